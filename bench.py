@@ -1,0 +1,484 @@
+"""Benchmark of the decode-time KV hot path: SIEVE miss detection + miss-row gather per
+layer-step, BASELINE config 2 (DSA/MLA decode: 64 requests x 8192-token context, 61 layers,
+topK 2048, hot buffer 4096 slots, miss ratio 0.2, 1152-byte fp16 rows N(0,1), seed 1).
+
+A step is one decode step: every layer runs sieve_update then the gather of its miss rows
+(the reference driver's per-layer sequence, xds/xds_decode.py:225-233). The metric is the
+reference's own: miss rows x 1152 B / (sieve + gather) time (xds_decode.py:226-233,280), in
+GB/s; p50/p99 microseconds per layer-step are reported beside it.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+At N=1 the pool is one segment in the GPU's own HBM. Under torchrun with N>1 ranks, every
+rank runs its own 64 requests (weak scaling) and its pool is striped S=1 over the other N-1
+GPUs' HBM (segments mapped through CUDA IPC, read in-kernel over NVLink/NVSwitch); there is no
+collective on the data path. `--impl reference` times the reference's CPU path (the C
+restatement of its sieve plus a host memcpy gather following its stripe map) on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+ROW_BYTES = 1152
+CFG = dict(name="c2_dsa_decode", requests=64, ctx=8192, layers=61, top_k=2048, dbs=4096, miss_ratio=0.2,
+           stripe_rows=1, seed=1)
+METRIC = "miss-row import GB/s (sieve+gather, per layer-step)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers per decode step (61 = config 2)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples (every 200 ms) over the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = open(os.path.join("/tmp", "kvb_clocks_{}.csv".format(os.getpid())), "w+")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.seek(0)
+        sm, mx, reasons = [], None, set()
+        for line in self.out.read().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(self.NAMES, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        self.out.close()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def pct(xs, q):
+    xs = sorted(xs)
+    if not xs:
+        return None
+    i = min(len(xs) - 1, max(0, int(round(q / 100.0 * (len(xs) - 1)))))
+    return xs[i]
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def state_bytes(padded, vis, ht_size):
+    """Bytes of one request's SIEVE state: token row, bitmap, table, hand word."""
+    return padded * 4 + vis + ht_size * 2 + 4
+
+
+def build_pool(mod, torch, dist, rank, world, local, L, layer_rows, seed):
+    """Segments of this rank's pool. N=1: one segment in own HBM. N>1: node i of rank h's pool
+    lives on the i-th GPU other than h; every rank allocates and fills the segments it hosts
+    and maps its own pool's segments from the other ranks through CUDA IPC handles."""
+    from kv_offload_proto_b200.pool import device_view, per_layer_seg_rows
+    nodes_of = (lambda h: [h]) if world == 1 else (lambda h: [g for g in range(world) if g != h])
+    n = len(nodes_of(rank))
+    seg_bytes = L * per_layer_seg_rows(layer_rows, n) * ROW_BYTES
+    hosted = {}
+    for h in range(world):
+        if world > 1 and h == rank:
+            continue
+        idx = nodes_of(h).index(rank)
+        addr = mod.segment_alloc(local, seg_bytes)
+        view = device_view(addr, seg_bytes, "cuda:{}".format(local)).view(torch.float16)
+        gen = torch.Generator(device="cuda:{}".format(local)).manual_seed(seed * 7919 + h * 131 + idx)
+        chunk = 1 << 29
+        for o in range(0, view.numel(), chunk):
+            view[o:o + chunk].normal_(generator=gen)
+        hosted[(h, idx)] = addr
+    if world == 1:
+        return [hosted[(rank, 0)]], nodes_of(rank), list(hosted.values()), []
+    handles = {k: mod.ipc_get_handle(a) for k, a in hosted.items()}
+    everyone = [None] * world
+    dist.all_gather_object(everyone, handles)
+    mine = [None] * n
+    for hd in everyone:
+        for (h, idx), hnd in hd.items():
+            if h == rank:
+                mine[idx] = mod.ipc_open_handle(local, hnd)
+    assert all(a is not None for a in mine)
+    return mine, nodes_of(rank), list(hosted.values()), list(mine)
+
+
+def run_b200(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    import kv_offload_proto_b200 as kp
+    from kv_offload_proto_b200.offload import XdsOffloadCoordinator
+    from kv_offload_proto_b200.pool import DevicePool
+    from kv_offload_proto_b200.workload import sample_topk_device
+
+    mod = kp.install_kvops_ext()
+    mod.init(local, "")
+    dev = torch.device("cuda", local)
+    R, ctx, K, dbs, miss = CFG["requests"], CFG["ctx"], CFG["top_k"], CFG["dbs"], CFG["miss_ratio"]
+    L = args.layers
+    layer_rows = R * ctx
+    W, S = args.warmup, args.steps
+    T = W + S
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    seg_addrs, nodes, hosted, opened = build_pool(mod, torch, dist, rank, world, local, L, layer_rows, CFG["seed"])
+    pool = DevicePool(local, L, layer_rows, ROW_BYTES, CFG["stripe_rows"], segment_devices=nodes,
+                      segment_addrs=seg_addrs)
+    co = XdsOffloadCoordinator(dev, L, R, dbs, K, R, ctx)
+    hot = torch.empty((L, R * dbs * ROW_BYTES), dtype=torch.uint8, device=dev)
+    pre, base = [ctx] * R, [r * ctx for r in range(R)]
+    co.admit_all(pre, base)
+    co.set_batch(torch.arange(R, dtype=torch.int64, device=dev), torch.full((R,), ctx, dtype=torch.int32, device=dev))
+
+    # Inputs: BASELINE config 2 draws (unique positions; hits from the current residents), made
+    # once by running the device SIEVE ahead; the replay below starts from the same admitted
+    # state, so every layer-step sees exactly the state its draw was made against.
+    gen = torch.Generator(device=dev).manual_seed(CFG["seed"] * 1000 + rank)
+    topk = torch.empty((T, L, R, K), dtype=torch.int32, device=dev)
+    misses = torch.zeros((T, L), dtype=torch.int64, device=dev)
+    for s in range(T):
+        for l in range(L):
+            topk[s, l] = sample_topk_device(co.device_buffer_tokens[l, :R], ctx, dbs, K, miss, gen)
+            co.sieve_update(l, topk[s, l])
+            misses[s, l] = co.is_miss.sum()
+    misses_h = misses.cpu().numpy()
+    co.admit_all(pre, base)
+
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def layer_step(s, l, ev=None):
+        if ev is not None:
+            ev[0].record()
+        co.sieve_update(l, topk[s, l], stream=stream)
+        if ev is not None:
+            ev[1].record()
+        pool.batch_read(l, topk[s, l], co._req_pool_indices, co.req_host_base, co.top_k_device_slots, co.is_miss,
+                        co.num_real, hot[l], R, K, stream, 1, fused=True, hot_req_stride_rows=dbs)
+        if ev is not None:
+            ev[2].record()
+
+    for s in range(W):
+        for l in range(L):
+            layer_step(s, l)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(S * L)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    torch.cuda.synchronize()
+    barrier()
+    t0.record()
+    for s in range(W, T):
+        for l in range(L):
+            layer_step(s, l, evs[(s - W) * L + l])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    last = int(co.is_miss.sum().item())
+    assert last == int(misses_h[T - 1, L - 1]), "replay diverged from the input pass"
+    elapsed = t0.elapsed_time(t1) * 1e-3
+    sieve_us = [e[0].elapsed_time(e[1]) * 1e3 for e in evs]
+    gather_us = [e[1].elapsed_time(e[2]) * 1e3 for e in evs]
+    step_us = [e[0].elapsed_time(e[2]) * 1e3 for e in evs]
+    miss_rows = int(misses_h[W:].sum())
+
+    e2e = None if args.no_e2e else run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev)
+
+    res = dict(elapsed=elapsed, miss_rows=miss_rows, sieve_us=sieve_us, gather_us=gather_us, step_us=step_us,
+               e2e=e2e, clocks=clk, nodes=len(nodes))
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, res)
+    else:
+        gathered = [res]
+    for a in opened:
+        mod.ipc_close_handle(a)
+    barrier()
+    for a in hosted:
+        mod.segment_free(a)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        report_b200(args, world, gathered, co)
+
+
+def run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev):
+    """The same decode steps through the public API with host inputs: each step copies its
+    topK tensors from pinned host memory, runs every layer's sieve_update + batch_read and waits
+    on the status slots (the reference driver's loop, xds_decode.py:226-236), then reads the
+    per-layer miss counts back to the host. Host wall clock around the K timed steps."""
+    T = W + S
+    topk_host = topk.cpu().pin_memory()
+    buf = torch.empty((L, R, K), dtype=torch.int32, device=dev)
+    counts = torch.zeros(L, dtype=torch.int64, device=dev)
+    counts_h = torch.zeros(L, dtype=torch.int64).pin_memory()
+    co.admit_all(pre, base)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(s):
+        buf.copy_(topk_host[s], non_blocking=True)
+        for l in range(L):
+            co.sieve_update(l, buf[l], stream=stream.cuda_stream)
+            st = pool.batch_read(l, buf[l], co._req_pool_indices, co.req_host_base, co.top_k_device_slots,
+                                 co.is_miss, co.num_real, hot[l], R, K, stream.cuda_stream, 1, fused=True,
+                                 hot_req_stride_rows=dbs)
+            pool.wait(st)
+            counts[l] = co.is_miss.sum()
+        counts_h.copy_(counts, non_blocking=True)
+        stream.synchronize()
+
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(W, T):
+        step(s)
+    dt = time.perf_counter() - t0
+    assert np.array_equal(counts_h.numpy(), misses_h[T - 1]), "e2e replay diverged"
+    rows = int(misses_h[W:].sum())
+    return {"value": rows * ROW_BYTES / dt / 1e9, "unit": "GB/s", "ms_per_step": dt * 1e3 / S,
+            "h2d_bytes_per_step": L * R * K * 4, "d2h_bytes_per_step": L * 8}
+
+
+def traffic_per_unit():
+    """DRAM bytes per unit measured by ncu (profiles/traffic.json), if captured."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return {}
+    with open(path) as f:
+        return json.load(f)
+
+
+def report_b200(args, world, gathered, co):
+    hbm_peak, peak_kind = peaks()
+    R, K = CFG["requests"], CFG["top_k"]
+    L = args.layers
+    elapsed = max(g["elapsed"] for g in gathered)
+    miss_rows = sum(g["miss_rows"] for g in gathered)
+    value = miss_rows * ROW_BYTES / elapsed / 1e9
+    g0 = gathered[0]
+    n = len(g0["sieve_us"])
+    sieve_avg = sum(g0["sieve_us"]) / n
+    gather_avg = sum(g0["gather_us"]) / n
+    rows_per_launch = g0["miss_rows"] / n
+    remote = world > 1
+    tr = traffic_per_unit()
+    # Gather: payload read + write (local pool) or NVLink ingress (peer pool), plus 9 B of
+    # metadata per position and 16 B per request.
+    meta = R * K * 9 + R * 16
+    if remote:
+        g_bytes, g_peak, g_bound, g_kind = rows_per_launch * ROW_BYTES, 770.0, "nvlink", "peer-copy 770 GB/s/dir"
+    else:
+        g_bytes, g_peak, g_bound, g_kind = rows_per_launch * 2 * ROW_BYTES + meta, hbm_peak, "hbm", peak_kind
+    sb = state_bytes(co.padded_buffer_size, co.visited_stride_b, co.ht_size)
+    s_bytes = R * (2 * sb + 9 * K)
+    roof_gather = {"kernel": "gather_kernel", "bound": g_bound, "achieved": g_bytes / (gather_avg * 1e-6) / 1e9,
+                   "peak": g_peak, "unit": "GB/s", "peak_source": g_kind,
+                   "traffic": tr["gather_per_row"] * rows_per_launch if "gather_per_row" in tr else None,
+                   "algorithmic_bytes": g_bytes, "avg_us": gather_avg}
+    roof_gather["frac"] = roof_gather["achieved"] / g_peak
+    roof_sieve = {"kernel": "sieve_update_kernel", "bound": "hbm", "achieved": s_bytes / (sieve_avg * 1e-6) / 1e9,
+                  "peak": hbm_peak, "unit": "GB/s", "peak_source": peak_kind,
+                  "traffic": tr["sieve_per_request"] * R if "sieve_per_request" in tr else None,
+                  "algorithmic_bytes": s_bytes, "avg_us": sieve_avg}
+    roof_sieve["frac"] = roof_sieve["achieved"] / hbm_peak
+    dominant, other = (roof_sieve, roof_gather) if sieve_avg >= gather_avg else (roof_gather, roof_sieve)
+    steps_all = [x for g in gathered for x in g["step_us"]]
+    out = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+        "config": {"workload": CFG["name"], "requests_per_gpu": R, "ctx": CFG["ctx"], "layers": L, "top_k": K,
+                   "hot_slots": CFG["dbs"], "miss_ratio": CFG["miss_ratio"], "row_bytes": ROW_BYTES,
+                   "stripe_rows": CFG["stripe_rows"],
+                   "pool": "local HBM segment" if not remote else "striped over the other {} GPUs' HBM".format(
+                       world - 1),
+                   "l2": "inputs larger than L2 (SIEVE state {:.0f} MB, pool {:.1f} GB per GPU)".format(
+                       L * R * sb / 1e6, L * R * CFG["ctx"] * ROW_BYTES / 1e9),
+                   "step": "one decode step = {} layers x (sieve_update + gather)".format(L)},
+        "p50_us_per_layer_step": pct(steps_all, 50), "p99_us_per_layer_step": pct(steps_all, 99),
+        "sieve_p50_us": pct(g0["sieve_us"], 50), "gather_p50_us": pct(g0["gather_us"], 50),
+        "gather_only_gbs": g0["miss_rows"] * ROW_BYTES / (sum(g0["gather_us"]) * 1e-6) / 1e9,
+        "miss_rows_per_layer_step": rows_per_launch,
+        "roofline": dominant, "roofline_other": other,
+        "gpu_launches": 2 * L * args.steps,
+        "clocks": g0["clocks"],
+    }
+    if g0["e2e"] is not None:
+        e = dict(g0["e2e"])
+        if world > 1:
+            e["value"] = sum(g["e2e"]["value"] for g in gathered)
+        out["e2e"] = e
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = run_cpu(layer_steps=8, warm=1)
+    print(json.dumps(out), flush=True)
+
+
+# ---- CPU legs: the reference's path on the host cores ------------------------------------
+
+def host_topk(rng, st, layer, R, K, ctx, miss_ratio):
+    """Config 2 draw from the checker's state: unique positions, hits from the residents."""
+    out = np.empty((R, K), np.int32)
+    n_miss = int(round(K * miss_ratio))
+    for r in range(R):
+        tok = st.tokens[layer, r, :st.dbs]
+        res = tok[(tok >= 0) & (tok < ctx)]
+        mask = np.ones(ctx, bool)
+        mask[res] = False
+        nonres = np.flatnonzero(mask)
+        row = np.concatenate([rng.choice(nonres, n_miss, replace=False), rng.choice(res, K - n_miss, replace=False)])
+        rng.shuffle(row)
+        out[r] = row
+    return out
+
+
+class CpuPath:
+    """The reference's CPU path on a bounded sample of config 2: each layer-step runs the
+    checker's sieve (kvoracle.c, threaded over requests) then a host memcpy gather following
+    the stripe map (threaded over positions), over `layers` layer states of 64 requests."""
+
+    def __init__(self, threads=None, layers=4):
+        import oracle
+        self.oracle = oracle
+        self.threads = threads or os.cpu_count() or 1
+        self.layers = layers
+        R, ctx, K, dbs = CFG["requests"], CFG["ctx"], CFG["top_k"], CFG["dbs"]
+        self.rng = np.random.default_rng(CFG["seed"])
+        self.st = oracle.SieveState(layers, R, dbs, K)
+        for r in range(R):
+            self.st.admit(r, ctx)
+        self.seg = np.frombuffer(self.rng.bytes(R * ctx * ROW_BYTES), dtype=np.uint8).copy()
+        self.hot = np.zeros(R * dbs * ROW_BYTES, np.uint8)
+        self.pool_idx, self.seq = np.arange(R, dtype=np.int64), np.full(R, ctx, np.int32)
+        self.base = np.arange(R, dtype=np.int64) * ctx
+        self.i = 0
+
+    def run(self, layer_steps):
+        """Returns (seconds, miss rows) of `layer_steps` timed layer-steps."""
+        R, ctx, K, dbs, miss = CFG["requests"], CFG["ctx"], CFG["top_k"], CFG["dbs"], CFG["miss_ratio"]
+        total, rows = 0.0, 0
+        for _ in range(layer_steps):
+            l = self.i % self.layers
+            self.i += 1
+            topk = host_topk(self.rng, self.st, l, R, K, ctx, miss)
+            t0 = time.perf_counter()
+            slots, is_miss = self.st.update(l, topk, self.pool_idx, self.seq, nthreads=self.threads)
+            n = self.oracle.gather_all([self.seg], 0, ROW_BYTES, topk, self.pool_idx, self.base, slots, is_miss, R,
+                                       self.hot, K, R, 1, hot_req_stride_rows=dbs, nthreads=self.threads)
+            total += time.perf_counter() - t0
+            rows += n
+        return total, rows
+
+    def describe(self, layer_steps):
+        return ("{} layer-steps of config 2 (64 req x 2048 topK, 20% miss) over {} layer states; sieve "
+                "(kvoracle.c) + memcpy gather, {} host threads".format(layer_steps, self.layers, self.threads))
+
+
+def run_cpu(layer_steps, warm=1):
+    cp = CpuPath()
+    cp.run(warm)
+    secs, rows = cp.run(layer_steps)
+    return {"value": rows * ROW_BYTES / secs / 1e9, "unit": "GB/s", "cores": cp.threads, "kind": "port",
+            "sample": cp.describe(layer_steps), "us_per_layer_step": secs * 1e6 / layer_steps}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    L = 8
+    cp = CpuPath()
+    for _ in range(args.warmup):
+        cp.run(L)
+    secs, rows = 0.0, 0
+    for _ in range(args.steps):
+        s, r = cp.run(L)
+        secs += s
+        rows += r
+    value = rows * ROW_BYTES / secs / 1e9
+    cb = {"value": value, "unit": "GB/s", "cores": cp.threads, "kind": "port",
+          "sample": "per step: " + cp.describe(L), "us_per_layer_step": secs * 1e6 / (L * args.steps)}
+    out = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": secs * 1e3 / args.steps, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+           "config": {"workload": CFG["name"], "requests_per_gpu": CFG["requests"], "ctx": CFG["ctx"],
+                      "top_k": CFG["top_k"], "hot_slots": CFG["dbs"], "miss_ratio": CFG["miss_ratio"],
+                      "row_bytes": ROW_BYTES, "step": "{} layer-steps (bounded CPU sample)".format(L)},
+           "impl": "reference", "cpu_baseline": cb,
+           "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -19,22 +19,31 @@ constexpr uint16_t kHtEmpty = 0;
 
 // ---- hash table on a token row (hisp_kernel_common.h:29-112) -------------------
 // Every probe loop is bounded by the table size: a well-formed table (load <= 0.5)
-// never reaches the bound; a corrupted one cannot hang the GPU.
+// never reaches the bound; a corrupted one cannot hang the GPU. An entry naming a slot
+// past the token row (possible only in a corrupted table) reads as token -1, which no
+// probed token equals, so it is never dereferenced.
 
-__device__ __forceinline__ int32_t ht_find(const uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask)
+__device__ __forceinline__ int32_t tok_of(const int32_t *tok, uint16_t e, int32_t padded)
+{
+    const int32_t s = static_cast<int32_t>(e) - 1;
+    return s < padded ? tok[s] : -1;
+}
+
+__device__ __forceinline__ int32_t ht_find(const uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask,
+                                           int32_t padded)
 {
     uint32_t idx = ht_hash(token) & mask;
     for (uint32_t n = 0; n <= mask; ++n) {
         const uint16_t e = ht[idx];
         if (e == kHtEmpty) return -1;
-        if (tok[static_cast<int32_t>(e) - 1] == token) return static_cast<int32_t>(e) - 1;
+        if (tok_of(tok, e, padded) == token) return static_cast<int32_t>(e) - 1;
         idx = (idx + 1) & mask;
     }
     return -1;
 }
 
 __device__ __forceinline__ void ht_insert(uint16_t *ht, const int32_t *tok, int32_t token, int32_t slot,
-                                          uint32_t mask)
+                                          uint32_t mask, int32_t padded)
 {
     uint32_t idx = ht_hash(token) & mask;
     for (uint32_t n = 0; n <= mask; ++n) {
@@ -43,20 +52,21 @@ __device__ __forceinline__ void ht_insert(uint16_t *ht, const int32_t *tok, int3
             ht[idx] = static_cast<uint16_t>(slot + 1);
             return;
         }
-        if (tok[static_cast<int32_t>(e) - 1] == token) return;  // first slot of a duplicate wins
+        if (tok_of(tok, e, padded) == token) return;  // first slot of a duplicate wins
         idx = (idx + 1) & mask;
     }
 }
 
 // Backward-shift deletion, Knuth 6.4 Algorithm R (hisp_kernel_common.h:64-94).
-__device__ __forceinline__ void ht_erase(uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask)
+__device__ __forceinline__ void ht_erase(uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask,
+                                         int32_t padded)
 {
     uint32_t idx = ht_hash(token) & mask;
     uint32_t n = 0;
     for (; n <= mask; ++n) {
         const uint16_t e = ht[idx];
         if (e == kHtEmpty) return;
-        if (tok[static_cast<int32_t>(e) - 1] == token) break;
+        if (tok_of(tok, e, padded) == token) break;
         idx = (idx + 1) & mask;
     }
     if (n > mask) return;
@@ -65,7 +75,7 @@ __device__ __forceinline__ void ht_erase(uint16_t *ht, const int32_t *tok, int32
         i = static_cast<int32_t>((static_cast<uint32_t>(i) + 1) & mask);
         const uint16_t e = ht[i];
         if (e == kHtEmpty) break;
-        const int32_t home = static_cast<int32_t>(ht_hash(tok[static_cast<int32_t>(e) - 1]) & mask);
+        const int32_t home = static_cast<int32_t>(ht_hash(tok_of(tok, e, padded)) & mask);
         const bool move = (j < i) ? (home <= j || home > i) : (home <= j && home > i);
         if (move) {
             ht[j] = e;
@@ -99,7 +109,7 @@ __device__ int32_t sieve_sequential(const int32_t *tp, int32_t K, int32_t *os, i
             om[k] = 0;
             continue;
         }
-        const int32_t hit = ht_find(ht, tok, t, mask);
+        const int32_t hit = ht_find(ht, tok, t, mask, padded);
         if (hit >= 0) {
             os[k] = hit;
             om[k] = 0;
@@ -112,8 +122,8 @@ __device__ int32_t sieve_sequential(const int32_t *tp, int32_t K, int32_t *os, i
             if (++h == dbs) h = 0;
         }
         const int32_t old = tok[h];
-        if (old >= 0) ht_erase(ht, tok, old, mask);
-        ht_insert(ht, tok, t, h, mask);
+        if (old >= 0) ht_erase(ht, tok, old, mask, padded);
+        ht_insert(ht, tok, t, h, mask, padded);
         d = true;
         os[k] = h;
         om[k] = 1;
@@ -263,7 +273,7 @@ __global__ void __launch_bounds__(kSieveThreads) sieve_ht_init_kernel(const HtIn
         if (threadIdx.x == 0) {
             for (int32_t s = 0; s < p.dbs; ++s) {
                 const int32_t t = s_tok[s];
-                if (t >= 0) ht_insert(s_ht, s_tok, t, s, mask);
+                if (t >= 0) ht_insert(s_ht, s_tok, t, s, mask, p.padded);
             }
         }
         __syncthreads();
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(kSieveThreads) sieve_ht_init_kernel(const HtIn
         if (threadIdx.x == 0) {
             for (int32_t s = 0; s < p.dbs; ++s) {
                 const int32_t t = g_tok[s];
-                if (t >= 0) ht_insert(g_ht, g_tok, t, s, mask);
+                if (t >= 0) ht_insert(g_ht, g_tok, t, s, mask, p.padded);
             }
         }
     }

@@ -15,7 +15,22 @@ from typing import List, Optional, Sequence
 from . import kvops as _kvops_module
 
 __all__ = ["DevicePool", "RowAllocator", "per_layer_seg_rows", "per_layer_seg_rows_injective", "node_of",
-           "seg_row_of"]
+           "seg_row_of", "device_view"]
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ wrapper of a raw UVA address (uint8, 1-D)."""
+
+    def __init__(self, addr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(addr, nbytes, device):
+    """uint8 torch tensor aliasing `nbytes` of device (or mapped host) memory at `addr`,
+    e.g. a segment from segment_alloc or an IPC mapping; the memory is not owned."""
+    import torch
+    return torch.as_tensor(_CudaArray(addr, nbytes), device=device)
 
 
 def per_layer_seg_rows(layer_rows, node_num):

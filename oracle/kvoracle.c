@@ -39,16 +39,24 @@ int64_t ko_ht_size(int64_t padded, int64_t top_k)
     return p;
 }
 
+/* Token held by the slot an entry names; an entry past the token row (only in a corrupted
+ * table) reads as -1, which no probed token equals. Same guard as the CUDA kernels. */
+static inline int32_t tok_of(const int32_t *tok, uint16_t e, int32_t padded)
+{
+    const int32_t s = (int32_t)e - 1;
+    return s < padded ? tok[s] : -1;
+}
+
 /* Probe for token; returns slot or -1: hisp_kernel_common.h:29-43. Bounded by
  * the table size so a corrupted table cannot spin forever (the reference
  * loop is unbounded; on a well-formed table at load <= 0.5 the bound is never hit). */
-static int32_t ht_find(const uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask)
+static int32_t ht_find(const uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask, int32_t padded)
 {
     uint32_t idx = ko_hash(token) & mask;
     for (uint32_t n = 0; n <= mask; n++) {
         uint16_t e = ht[idx];
         if (e == 0) return -1;
-        if (tok[(int32_t)e - 1] == token) return (int32_t)e - 1;
+        if (tok_of(tok, e, padded) == token) return (int32_t)e - 1;
         idx = (idx + 1) & mask;
     }
     return -1;
@@ -56,7 +64,8 @@ static int32_t ht_find(const uint16_t *ht, const int32_t *tok, int32_t token, ui
 
 /* Insert token->slot, first (lowest-probe) entry of a duplicate token wins:
  * hisp_kernel_common.h:46-61 (and the GM-token twin at :97-112). */
-static void ht_insert(uint16_t *ht, const int32_t *tok, int32_t token, int32_t slot, uint32_t mask)
+static void ht_insert(uint16_t *ht, const int32_t *tok, int32_t token, int32_t slot, uint32_t mask,
+                      int32_t padded)
 {
     uint32_t idx = ko_hash(token) & mask;
     for (uint32_t n = 0; n <= mask; n++) {
@@ -65,7 +74,7 @@ static void ht_insert(uint16_t *ht, const int32_t *tok, int32_t token, int32_t s
             ht[idx] = (uint16_t)(slot + 1);
             return;
         }
-        if (tok[(int32_t)e - 1] == token) return;
+        if (tok_of(tok, e, padded) == token) return;
         idx = (idx + 1) & mask;
     }
 }
@@ -73,14 +82,14 @@ static void ht_insert(uint16_t *ht, const int32_t *tok, int32_t token, int32_t s
 /* Backward-shift deletion (Knuth 6.4 Algorithm R): hisp_kernel_common.h:64-94.
  * The move test for the entry at i with home h against the gap j is
  * (j < i) ? (h <= j || h > i) : (h <= j && h > i)   (:87). */
-static void ht_erase(uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask)
+static void ht_erase(uint16_t *ht, const int32_t *tok, int32_t token, uint32_t mask, int32_t padded)
 {
     uint32_t idx = ko_hash(token) & mask;
     uint32_t n;
     for (n = 0; n <= mask; n++) {
         uint16_t e = ht[idx];
         if (e == 0) return;
-        if (tok[(int32_t)e - 1] == token) break;
+        if (tok_of(tok, e, padded) == token) break;
         idx = (idx + 1) & mask;
     }
     if (n > mask) return;
@@ -89,7 +98,7 @@ static void ht_erase(uint16_t *ht, const int32_t *tok, int32_t token, uint32_t m
         i = (int32_t)(((uint32_t)i + 1) & mask);
         uint16_t e = ht[i];
         if (e == 0) break;
-        int32_t home = (int32_t)(ko_hash(tok[(int32_t)e - 1]) & mask);
+        int32_t home = (int32_t)(ko_hash(tok_of(tok, e, padded)) & mask);
         int move = (j < i) ? (home <= j || home > i) : (home <= j && home > i);
         if (move) {
             ht[j] = e;
@@ -151,7 +160,7 @@ static void sieve_row(const SieveJob *J, int32_t bid)
         const int32_t t = tp[k];
         if (t < 0 || t >= seq_len) { os[k] = -1; om[k] = 0; continue; }
         if (t >= prefill) { os[k] = J->padded + (t - prefill); om[k] = 0; continue; }
-        const int32_t hit = ht_find(ht, tok, t, mask);
+        const int32_t hit = ht_find(ht, tok, t, mask, J->padded);
         if (hit >= 0) { os[k] = hit; om[k] = 0; vis_set(vis, hit); continue; }
         int32_t h = hand;
         while (vis_get(vis, h)) { /* hand sweep: :139-146 */
@@ -159,8 +168,8 @@ static void sieve_row(const SieveJob *J, int32_t bid)
             if (++h == dbs) h = 0;
         }
         const int32_t old = tok[h];
-        if (old >= 0) ht_erase(ht, tok, old, mask); /* :148-151 */
-        ht_insert(ht, tok, t, h, mask);              /* :152 (before tok[h] is updated) */
+        if (old >= 0) ht_erase(ht, tok, old, mask, J->padded); /* :148-151 */
+        ht_insert(ht, tok, t, h, mask, J->padded);   /* :152 (before tok[h] is updated) */
         os[k] = h;
         om[k] = 1;
         tok[h] = t;
@@ -228,7 +237,7 @@ int ko_sieve_ht_init(const int32_t *tokens3d, uint16_t *ht3d, int32_t req_start,
         uint16_t *ht = ht3d + (layer * pool_size + req) * ht_size;
         memset(ht, 0, sizeof(uint16_t) * (size_t)ht_size);
         for (int32_t s = 0; s < dbs; s++)
-            if (tok[s] >= 0) ht_insert(ht, tok, tok[s], s, mask);
+            if (tok[s] >= 0) ht_insert(ht, tok, tok[s], s, mask, padded);
     }
     return 0;
 }
