@@ -2,11 +2,12 @@
 // (hisp_sieve_ht_init) for sm_100a.
 //
 // One CTA per batch row (request). The request's state — token row, visited bitmap,
-// uint16 open-addressing table and hand — is staged in shared memory when it fits
-// the per-CTA opt-in limit and updated in place in global memory otherwise. The
-// SIEVE itself runs in the reference's strict position order
-// (hisp_sieve_update.cpp:115-163), so outputs and the persisted state (including
-// the hash-table bytes) are identical to the reference kernel's.
+// uint16 open-addressing table and hand — is staged in shared memory. The default kernel
+// (sieve_fast_kernel) computes the step in parallel phases that reproduce the reference's
+// strict position order (hisp_sieve_update.cpp:115-163) exactly; steps outside its
+// assumptions, and states too large for shared memory, run the position-ordered loop
+// itself (sieve_sequential), staged or in place in global memory. Either way the outputs
+// and the persisted state (including the hash-table bytes) equal the reference kernel's.
 #include <stdint.h>
 
 #include "kvops_internal.cuh"
@@ -290,6 +291,497 @@ __global__ void __launch_bounds__(kSieveThreads) sieve_ht_init_kernel(const HtIn
     }
 }
 
+// ==== Parallel exact path ===========================================================
+//
+// The same step as sieve_sequential, computed in phases instead of position order:
+//  1. every position probes the step-initial table in parallel; for each hot slot the first
+//     and last position that looks up its resident token are recorded (Tf, Tl); tokens that
+//     are not resident are de-duplicated, their first occurrences are the initial misses;
+//  2. one warp replays the hand sweep: misses are taken in position order and each one evicts
+//     the next slot (from the hand) whose visited bit is clear and whose token is not looked
+//     up before that miss (bit clear and Tf > miss); evicting a slot whose token is looked up
+//     later turns that later lookup into a miss (Tf is queued). 32 slots are tested per ballot;
+//  3. outputs, final visited bits and the new hand follow in parallel;
+//  4. the table is updated in two parallel passes: the evicted tokens are deleted (each
+//     affected probe run is re-packed from its first deleted cell, which is what
+//     backward-shift deletion produces), then the new tokens are inserted with priority
+//     = miss position (cells are claimed by 16-bit CAS; an earlier miss displaces a later
+//     one). Linear probing with backward-shift deletion leaves the table exactly as if the
+//     surviving keys had been inserted in order, so this equals the reference's
+//     erase/insert sequence byte for byte.
+// Phase 2 assumes the sweep passes no slot twice in one step, and phase 4 assumes the table
+// maps each resident token to exactly its slot (true of any state these kernels or the
+// reference build). A step that breaks either assumption is detected before anything is
+// written back and is recomputed by the sequential path from the untouched global state.
+
+constexpr int kFastThreads = 512;
+constexpr uint16_t kNone16 = 0xFFFFu;
+constexpr uint16_t kDelMark = 0xFFFFu;   // table cell: deleted entry (entries are <= 65520)
+constexpr uint16_t kLeadMark = 0xFFFEu;  // table cell: first deleted entry of its probe run
+constexpr uint8_t kClsNone = 0, kClsRes = 1, kClsNew = 2, kClsPending = 3, kClsPlaced = 4;
+
+struct FastLayout {
+    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, missb, total;
+    int32_t dcap;
+};
+
+__host__ __device__ __forceinline__ size_t take(size_t *o, size_t bytes)
+{
+    const size_t r = *o;
+    *o = align_up(*o + bytes, 16);
+    return r;
+}
+
+__host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32_t ht_size, int32_t vis_stride,
+                                                           int32_t K, int32_t dbs)
+{
+    FastLayout L;
+    L.dcap = 1;
+    while (L.dcap < 2 * K) L.dcap <<= 1;
+    size_t o = 0;
+    L.ht = take(&o, 2ull * ht_size);
+    L.tok = take(&o, 4ull * padded);
+    L.topk = take(&o, 4ull * K);
+    L.os = take(&o, 4ull * K);
+    L.om = take(&o, static_cast<size_t>(K));
+    L.cls = take(&o, static_cast<size_t>(K));
+    L.aux = take(&o, 2ull * K);
+    L.tf = take(&o, 4ull * dbs);
+    L.evt = take(&o, 2ull * padded);
+    L.vini = take(&o, static_cast<size_t>(vis_stride));
+    L.vfin = take(&o, static_cast<size_t>(vis_stride));
+    L.dkey = take(&o, 4ull * L.dcap);
+    L.dfirst = take(&o, 4ull * L.dcap);
+    L.missb = take(&o, 4ull * ((K + 31) / 32));
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ void put_bit(uint32_t *words, int32_t c, bool v)
+{
+    if (v) atomicOr(&words[c >> 5], 1u << (c & 31));
+    else atomicAnd(&words[c >> 5], ~(1u << (c & 31)));
+}
+
+// Next queued miss position after `cur` (K if none).
+__device__ __forceinline__ int32_t next_miss(const uint32_t *missb, int32_t K, int32_t cur)
+{
+    const int32_t n = cur + 1;
+    if (n >= K) return K;
+    const int32_t nw = (K + 31) >> 5;
+    int32_t w = n >> 5;
+    uint32_t bits = missb[w] & (0xFFFFFFFFu << (n & 31));
+    while (bits == 0) {
+        if (++w >= nw) return K;
+        bits = missb[w];
+    }
+    return (w << 5) + __ffs(bits) - 1;
+}
+
+// Phase 2, one warp: replay the hand sweep over the hot slots. Returns false when the sweep
+// would pass a slot twice (the sequential path then takes the step).
+__device__ bool sweep_warp(const uint32_t *vini, uint32_t *vfin, const uint32_t *tf, uint16_t *evt,
+                           uint32_t *missb, int32_t *os, int8_t *om, int32_t K, int32_t dbs, int32_t hand0,
+                           int32_t *hand_out)
+{
+    const int lane = threadIdx.x & 31;
+    int32_t cur = next_miss(missb, K, -1);
+    int32_t cbase = hand0, passed0 = 0, pos = 0, last = -1;
+    int32_t c = 0;
+    bool valid = false;
+    uint32_t ib = 1, tfv = kNone16, tlv = 0;
+    auto load = [&]() {
+        c = cbase + lane;
+        while (c >= dbs) c -= dbs;
+        valid = passed0 + lane < dbs;
+        ib = valid ? (vini[c >> 5] >> (c & 31)) & 1u : 1u;
+        const uint32_t w = valid ? tf[c] : kNone16;
+        tfv = w & 0xFFFFu;
+        tlv = w >> 16;
+    };
+    auto advance = [&]() {
+        passed0 += 32;
+        cbase += 32;
+        while (cbase >= dbs) cbase -= dbs;
+        pos = 0;
+        load();
+    };
+    load();
+    bool ok = true;
+    while (cur < K) {
+        const bool elig = valid && lane >= pos && ib == 0 && tfv > static_cast<uint32_t>(cur);
+        const unsigned E = __ballot_sync(0xFFFFFFFFu, elig);
+        if (E == 0) {
+            if (!__all_sync(0xFFFFFFFFu, valid)) {  // every remaining slot already passed: wrap
+                ok = false;
+                break;
+            }
+            if (lane >= pos) put_bit(vfin, c, tfv != kNone16 && tlv > static_cast<uint32_t>(cur));
+            advance();
+            continue;
+        }
+        const int j = __ffs(E) - 1;
+        if (lane >= pos && lane < j) put_bit(vfin, c, tfv != kNone16 && tlv > static_cast<uint32_t>(cur));
+        if (lane == j) {  // evict slot c at miss `cur`
+            os[cur] = c;
+            om[cur] = 1;
+            evt[c] = static_cast<uint16_t>(cur);
+            put_bit(vfin, c, true);
+            if (tfv != kNone16) atomicOr(&missb[tfv >> 5], 1u << (tfv & 31));  // its token's first lookup misses
+        }
+        last = __shfl_sync(0xFFFFFFFFu, c, j);
+        pos = j + 1;
+        if (pos == 32) advance();
+        __syncwarp();
+        cur = next_miss(missb, K, cur);
+    }
+    if (ok && last >= 0) *hand_out = last + 1 == dbs ? 0 : last + 1;
+    return ok;
+}
+
+__global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const SieveParams p)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int s_flag;     // nonzero: recompute this step with the sequential path
+    __shared__ int s_changed[2];  // per-round progress flags, used alternately
+    __shared__ int s_any_miss;
+    __shared__ int32_t s_hand;
+    __shared__ bool s_dirty;
+    const int32_t bid = blockIdx.x;
+    const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    int32_t *g_slots = p.out_slots + static_cast<int64_t>(bid) * K;
+    int8_t *g_miss = p.is_miss + static_cast<int64_t>(bid) * K;
+
+    int32_t num_real = *p.num_real;
+    if (num_real > p.max_num_reqs) num_real = p.max_num_reqs;  // hisp_sieve_update.cpp:31-34
+    const int64_t req = bid < num_real ? p.req_pool[bid] : -1;
+    if (bid >= num_real || req < 0 || req >= p.pool_size) {  // :72-88
+        fill_dummy(g_slots, g_miss, K);
+        return;
+    }
+    const int32_t seq_len = p.seq_lens[bid];
+    const int32_t prefill = p.prefill[req];
+    const int32_t *g_topk = p.topk + static_cast<int64_t>(bid) * K;
+    int32_t *g_tok = p.tokens + req * padded;
+    uint8_t *g_vis = p.visited + req * p.vis_stride;
+    uint16_t *g_ht = p.ht + req * p.ht_size;
+    int32_t *g_hand = p.hand + req * kHandStride;
+    const uint32_t mask = static_cast<uint32_t>(p.ht_size) - 1u;
+
+    const FastLayout L = fast_layout(padded, p.ht_size, p.vis_stride, K, dbs);
+    uint16_t *s_ht = reinterpret_cast<uint16_t *>(smem + L.ht);
+    int32_t *s_tok = reinterpret_cast<int32_t *>(smem + L.tok);
+    int32_t *s_topk = reinterpret_cast<int32_t *>(smem + L.topk);
+    int32_t *s_os = reinterpret_cast<int32_t *>(smem + L.os);
+    int8_t *s_om = reinterpret_cast<int8_t *>(smem + L.om);
+    uint8_t *s_cls = reinterpret_cast<uint8_t *>(smem + L.cls);
+    uint16_t *s_aux = reinterpret_cast<uint16_t *>(smem + L.aux);
+    uint32_t *s_tf = reinterpret_cast<uint32_t *>(smem + L.tf);  // (Tl << 16) | Tf per hot slot
+    uint16_t *s_evt = reinterpret_cast<uint16_t *>(smem + L.evt);
+    uint32_t *s_vini = reinterpret_cast<uint32_t *>(smem + L.vini);
+    uint32_t *s_vfin = reinterpret_cast<uint32_t *>(smem + L.vfin);
+    int32_t *s_dkey = reinterpret_cast<int32_t *>(smem + L.dkey);
+    int32_t *s_dfirst = reinterpret_cast<int32_t *>(smem + L.dfirst);
+    uint32_t *s_missb = reinterpret_cast<uint32_t *>(smem + L.missb);
+    const uint32_t dmask = static_cast<uint32_t>(L.dcap) - 1u;
+
+    // ---- phase 0: stage the request's state, clear the step arrays ----
+    coop_copy(s_ht, g_ht, 2ull * p.ht_size);
+    coop_copy(s_tok, g_tok, 4ull * padded);
+    coop_copy(s_topk, g_topk, 4ull * K);
+    coop_copy(s_vini, g_vis, p.vis_stride);
+    coop_copy(s_vfin, g_vis, p.vis_stride);
+    for (int32_t i = tid; i < dbs; i += nt) s_tf[i] = kNone16;  // Tf = none, Tl = 0
+    for (int32_t i = tid; i < padded; i += nt) s_evt[i] = kNone16;
+    for (int32_t i = tid; i < L.dcap; i += nt) {
+        s_dkey[i] = -1;
+        s_dfirst[i] = 0x7FFFFFFF;
+    }
+    for (int32_t i = tid; i < (K + 31) / 32; i += nt) s_missb[i] = 0u;
+    if (tid == 0) {
+        int32_t hand = *g_hand;
+        if (hand < 0 || hand >= dbs) hand = 0;  // :108-111
+        s_hand = hand;
+        s_flag = 0;
+        s_any_miss = 0;
+        s_changed[0] = s_changed[1] = 0;
+    }
+    __syncthreads();
+
+    // ---- phase 1: classify and probe every position against the step-initial table ----
+    for (int32_t k = tid; k < K; k += nt) {
+        const int32_t t = s_topk[k];
+        s_cls[k] = kClsNone;
+        if (t < 0 || t >= seq_len) {
+            s_os[k] = -1;
+            s_om[k] = 0;
+            continue;
+        }
+        if (t >= prefill) {
+            s_os[k] = padded + (t - prefill);
+            s_om[k] = 0;
+            continue;
+        }
+        const int32_t s0 = ht_find(s_ht, s_tok, t, mask, padded);
+        if (s0 >= 0) {
+            if (s0 >= dbs) {  // a table entry outside the hot slots: not a state these kernels build
+                s_flag = 1;
+                continue;
+            }
+            s_cls[k] = kClsRes;
+            s_aux[k] = static_cast<uint16_t>(s0);
+            uint32_t old = s_tf[s0], assumed;
+            do {
+                assumed = old;
+                const uint32_t f = min(assumed & 0xFFFFu, static_cast<uint32_t>(k));
+                const uint32_t l = max(assumed >> 16, static_cast<uint32_t>(k));
+                const uint32_t nw = (l << 16) | f;
+                if (nw == assumed) break;
+                old = atomicCAS(&s_tf[s0], assumed, nw);
+            } while (old != assumed);
+        } else {
+            s_cls[k] = kClsNew;
+            uint32_t d = ht_hash(t) & dmask;
+            for (uint32_t n = 0; n <= dmask; ++n) {
+                const int32_t prev = atomicCAS(&s_dkey[d], -1, t);
+                if (prev == -1 || prev == t) {
+                    atomicMin(&s_dfirst[d], k);
+                    break;
+                }
+                d = (d + 1) & dmask;
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_flag) {
+        for (int32_t k = tid; k < K; k += nt) {
+            if (s_cls[k] != kClsNew) continue;
+            const int32_t t = s_topk[k];
+            uint32_t d = ht_hash(t) & dmask;
+            for (uint32_t n = 0; n <= dmask && s_dkey[d] != t; ++n) d = (d + 1) & dmask;
+            const int32_t f = s_dfirst[d];
+            s_aux[k] = static_cast<uint16_t>(f);
+            if (f == k) atomicOr(&s_missb[k >> 5], 1u << (k & 31));  // first lookup of a new token
+        }
+        for (int32_t c = tid; c < dbs; c += nt)  // default final bit: initial bit, or a hit this step
+            if ((s_tf[c] & 0xFFFFu) != kNone16) atomicOr(&s_vfin[c >> 5], 1u << (c & 31));
+    }
+    __syncthreads();
+
+    // ---- phase 2: the hand sweep, one warp ----
+    if (!s_flag && tid < 32) {
+        int32_t hand = s_hand;
+        const bool ok = sweep_warp(s_vini, s_vfin, s_tf, s_evt, s_missb, s_os, s_om, K, dbs, s_hand, &hand);
+        if (tid == 0) {
+            if (!ok) s_flag = 1;
+            s_hand = hand;
+            s_any_miss = next_miss(s_missb, K, -1) < K;
+        }
+    }
+    __syncthreads();
+
+    // ---- phase 3: table check for the evicted tokens; outputs of the hits ----
+    if (!s_flag) {
+        for (int32_t c = tid; c < dbs; c += nt) {
+            if (s_evt[c] == kNone16) continue;
+            const int32_t t = s_tok[c];
+            if (t < 0) continue;
+            // The first entry holding t must name slot c, and no second entry may follow.
+            uint32_t idx = ht_hash(t) & mask;
+            int32_t found = -1;
+            bool ended = false, dup = false;
+            for (uint32_t n = 0; n <= mask; ++n) {
+                const uint16_t e = s_ht[idx];
+                if (e == kHtEmpty) {
+                    ended = true;
+                    break;
+                }
+                if (tok_of(s_tok, e, padded) == t) {
+                    if (found >= 0) {
+                        dup = true;
+                        break;
+                    }
+                    found = static_cast<int32_t>(e) - 1;
+                }
+                idx = (idx + 1) & mask;
+            }
+            if (found != c || dup || !ended) s_flag = 1;
+        }
+        for (int32_t k = tid; k < K; k += nt) {
+            const uint8_t cls = s_cls[k];
+            if (cls == kClsRes) {
+                const int32_t s0 = s_aux[k];
+                if (s_evt[s0] != kNone16) {  // evicted before its first lookup, which became a miss
+                    const int32_t T = static_cast<int32_t>(s_tf[s0] & 0xFFFFu);
+                    if (k != T) {
+                        s_os[k] = s_os[T];
+                        s_om[k] = 0;
+                    }
+                } else {
+                    s_os[k] = s0;
+                    s_om[k] = 0;
+                }
+            } else if (cls == kClsNew) {
+                const int32_t k0 = s_aux[k];
+                if (k != k0) {
+                    s_os[k] = s_os[k0];
+                    s_om[k] = 0;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- phase 4: delete the evicted tokens from the table, re-packing each probe run ----
+    const bool update_table = !s_flag && s_any_miss;
+    if (update_table) {
+        for (int32_t c = tid; c < dbs; c += nt) {
+            if (s_evt[c] == kNone16 || s_tok[c] < 0) continue;
+            uint32_t idx = ht_hash(s_tok[c]) & mask;
+            for (uint32_t n = 0; n <= mask; ++n) {
+                if (s_ht[idx] == static_cast<uint16_t>(c + 1)) {
+                    s_ht[idx] = kDelMark;
+                    break;
+                }
+                idx = (idx + 1) & mask;
+            }
+        }
+    }
+    __syncthreads();
+    if (update_table) {  // the first deleted cell of each run leads its re-pack
+        for (uint32_t i = tid; i <= mask; i += nt) {
+            if (s_ht[i] != kDelMark) continue;
+            uint32_t j = (i - 1) & mask;
+            bool lead = true;
+            for (uint32_t n = 0; n <= mask; ++n) {
+                const uint16_t e = s_ht[j];
+                if (e == kHtEmpty) break;
+                if (e == kDelMark || e == kLeadMark) {
+                    lead = false;
+                    break;
+                }
+                j = (j - 1) & mask;
+            }
+            if (lead) s_ht[i] = kLeadMark;
+        }
+    }
+    __syncthreads();
+    if (update_table) {
+        for (uint32_t i = tid; i <= mask; i += nt) {
+            if (s_ht[i] != kLeadMark) continue;
+            // Walk the run from its first deleted cell; every surviving entry moves to the
+            // first empty cell from its home, which is never past its old cell.
+            uint32_t e = i;
+            for (uint32_t n = 0; n <= mask; ++n) {
+                const uint16_t v = s_ht[e];
+                if (v == kHtEmpty) break;
+                s_ht[e] = kHtEmpty;
+                if (v != kDelMark && v != kLeadMark) {
+                    uint32_t q = ht_hash(tok_of(s_tok, v, padded)) & mask;
+                    for (uint32_t m = 0; m <= mask && s_ht[q] != kHtEmpty; ++m) q = (q + 1) & mask;
+                    s_ht[q] = v;
+                }
+                e = (e + 1) & mask;
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
+    if (update_table) {
+        for (int32_t m = tid; m < K; m += nt) {
+            if ((s_missb[m >> 5] >> (m & 31)) & 1u) {
+                s_aux[m] = static_cast<uint16_t>(ht_hash(s_topk[m]) & mask);
+                s_cls[m] = kClsPending;
+            } else {
+                s_cls[m] = kClsNone;
+            }
+        }
+    }
+    __syncthreads();
+    if (update_table) {
+        const int32_t limit = 4 * p.ht_size + 64;
+        for (int32_t round = 0;; ++round) {
+            // Round r raises s_changed[r & 1]; thread 0 clears the other flag once every thread
+            // has passed the first barrier of round r, i.e. after all reads of round r-1's flag.
+            bool ch = false;
+            for (int32_t m = tid; m < K; m += nt) {
+                if (s_cls[m] != kClsPending) continue;
+                const uint16_t entry = static_cast<uint16_t>(s_os[m] + 1);
+                const uint32_t at = s_aux[m];
+                const uint16_t e = s_ht[at];
+                ch = true;
+                if (e == kHtEmpty) {
+                    if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), kHtEmpty, entry) == kHtEmpty)
+                        s_cls[m] = kClsPlaced;
+                } else {
+                    const int32_t es = static_cast<int32_t>(e) - 1;
+                    const uint16_t te = es < padded ? s_evt[es] : kNone16;
+                    if (te == kNone16 || te < m) {
+                        s_aux[m] = static_cast<uint16_t>((at + 1) & mask);
+                    } else if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), e, entry) == e) {
+                        s_cls[m] = kClsPlaced;  // the later miss it displaced moves on
+                    }
+                }
+            }
+            __syncthreads();
+            if (tid == 0) s_changed[(round + 1) & 1] = 0;
+            for (int32_t m = tid; m < K; m += nt) {
+                if (s_cls[m] == kClsPlaced && s_ht[s_aux[m]] != static_cast<uint16_t>(s_os[m] + 1)) {
+                    s_cls[m] = kClsPending;
+                    s_aux[m] = static_cast<uint16_t>((s_aux[m] + 1) & mask);
+                    ch = true;
+                }
+            }
+            if (ch) s_changed[round & 1] = 1;
+            __syncthreads();
+            if (!s_changed[round & 1]) break;
+            if (round > limit) {  // cannot happen on a table at load <= 0.5; recompute if it does
+                if (tid == 0) s_flag = 1;
+                __syncthreads();
+                break;
+            }
+        }
+    }
+    __syncthreads();
+
+    if (!s_flag) {
+        // ---- phase 6: write back ----
+        for (int32_t m = tid; m < K; m += nt)
+            if ((s_missb[m >> 5] >> (m & 31)) & 1u) g_tok[s_os[m]] = s_topk[m];
+        coop_copy(g_slots, s_os, 4ull * K);
+        coop_copy(g_miss, s_om, static_cast<size_t>(K));
+        coop_copy(g_vis, s_vfin, p.vis_stride);
+        if (s_any_miss) coop_copy(g_ht, s_ht, 2ull * p.ht_size);
+        if (tid == 0) *g_hand = s_hand;
+        return;
+    }
+
+    // ---- exact sequential path from the untouched global state ----
+    coop_copy(s_ht, g_ht, 2ull * p.ht_size);
+    coop_copy(s_tok, g_tok, 4ull * padded);
+    coop_copy(s_vfin, g_vis, p.vis_stride);
+    __syncthreads();
+    if (tid == 0) {
+        int32_t hand = *g_hand;
+        if (hand < 0 || hand >= dbs) hand = 0;
+        bool dirty = false;
+        s_hand = sieve_sequential(s_topk, K, s_os, s_om, s_tok, reinterpret_cast<uint8_t *>(s_vfin), s_ht, mask, dbs,
+                                  padded, seq_len, prefill, hand, &dirty);
+        s_dirty = dirty;
+    }
+    __syncthreads();
+    coop_copy(g_slots, s_os, 4ull * K);
+    coop_copy(g_miss, s_om, static_cast<size_t>(K));
+    coop_copy(g_vis, s_vfin, p.vis_stride);
+    if (s_dirty) {
+        coop_copy(g_tok, s_tok, 4ull * padded);
+        coop_copy(g_ht, s_ht, 2ull * p.ht_size);
+    }
+    if (tid == 0) *g_hand = s_hand;
+}
+
 int max_optin_smem()
 {
     int dev = 0, v = 0;
@@ -303,8 +795,19 @@ int max_optin_smem()
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int /*sm_count*/)
 {
     if (p.max_num_reqs <= 0) return cudaSuccess;
-    const SmemLayout L = sieve_smem_layout(p.padded, p.ht_size, p.vis_stride, p.top_k);
     const int limit = max_optin_smem();
+    // Parallel path: positions and slots must fit its 16-bit bookkeeping.
+    if (p.top_k <= 65535 && p.ht_size <= 65536 && p.dbs <= 65535) {
+        const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
+        if (F.total <= static_cast<size_t>(limit)) {
+            cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(F.total));
+            if (e != cudaSuccess) return e;
+            sieve_fast_kernel<<<p.max_num_reqs, kFastThreads, F.total, s>>>(p);
+            return cudaGetLastError();
+        }
+    }
+    const SmemLayout L = sieve_smem_layout(p.padded, p.ht_size, p.vis_stride, p.top_k);
     if (L.total <= static_cast<size_t>(limit)) {
         cudaError_t e = cudaFuncSetAttribute(sieve_update_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(L.total));

@@ -165,3 +165,47 @@ def test_sieve_update_validation(kw, msg):
     with pytest.raises(RuntimeError, match=msg):
         mod.sieve_update(8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 64, a["dbs"], a["padded"], a["vis"], 1, 1, 0,
                          a["block_dim"])
+
+
+@pytest.mark.parametrize("dbs,K", [(300, 100), (4096, 2048)])
+def test_duplicate_token_state_matches_oracle(dbs, K):
+    """A token row holding the same token twice (only its first slot is in the table) is
+    outside the parallel path's assumptions: such steps must still match the reference."""
+    kv()
+    R = 3
+    rng = np.random.default_rng(dbs * 7)
+    prefill = max(2 * dbs, 3 * K)
+    st = oracle.SieveState(1, R, dbs, K)
+    for r in range(R):
+        st.admit(r, prefill)
+    st.tokens[0, :, 5] = st.tokens[0, :, 2]
+    st.tokens[0, :, 9] = st.tokens[0, :, 7]
+    ds = DeviceSieve(st)
+    for s in range(6):
+        topk = config_topk(rng, st, 0, np.arange(R), K, 0.3)
+        seq = np.full(R, prefill, np.int32)
+        got = ds.update(0, topk, np.arange(R), seq)
+        exp = st.update(0, topk, np.arange(R), seq)
+        np.testing.assert_array_equal(got[1], exp[1])
+        np.testing.assert_array_equal(got[0], exp[0])
+        ds.assert_state_equal()
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_c2_shape_many_steps(seed):
+    """Config-2 shape, 12 steps at 20% and 60% misses: long runs through the parallel path."""
+    kv()
+    R, dbs, K = 4, 4096, 2048
+    rng = np.random.default_rng(100 + seed)
+    st = oracle.SieveState(1, R, dbs, K)
+    for r in range(R):
+        st.admit(r, 8192)
+    ds = DeviceSieve(st)
+    for s in range(12):
+        topk = config_topk(rng, st, 0, np.arange(R), K, 0.2 if s % 3 else 0.6)
+        seq = np.full(R, 8192, np.int32)
+        got = ds.update(0, topk, np.arange(R), seq)
+        exp = st.update(0, topk, np.arange(R), seq)
+        np.testing.assert_array_equal(got[1], exp[1])
+        np.testing.assert_array_equal(got[0], exp[0])
+    ds.assert_state_equal()
