@@ -156,6 +156,26 @@ __device__ __forceinline__ void coop_copy(void *dst, const void *src, size_t byt
     }
 }
 
+// Asynchronous global -> shared staging: 16-byte cp.async when both sides allow it (all
+// copies of a phase stay in flight together; cp_async_wait_all() ends the phase), plain
+// cooperative copies otherwise.
+__device__ __forceinline__ void stage_async(void *dst_smem, const void *src, size_t bytes)
+{
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dst_smem) | reinterpret_cast<uintptr_t>(src);
+    if (((a | bytes) & 15) != 0) {
+        coop_copy(dst_smem, src, bytes);
+        return;
+    }
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+    const char *g = static_cast<const char *>(src);
+    for (size_t i = threadIdx.x; i < bytes / 16; i += blockDim.x)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + static_cast<uint32_t>(i * 16)),
+                     "l"(g + i * 16)
+                     : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void fill_dummy(int32_t *os, int8_t *om, int32_t K)
 {
     for (int32_t k = threadIdx.x; k < K; k += blockDim.x) {
@@ -357,12 +377,6 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
     return L;
 }
 
-__device__ __forceinline__ void put_bit(uint32_t *words, int32_t c, bool v)
-{
-    if (v) atomicOr(&words[c >> 5], 1u << (c & 31));
-    else atomicAnd(&words[c >> 5], ~(1u << (c & 31)));
-}
-
 // Next queued miss position after `cur` (K if none).
 __device__ __forceinline__ int32_t next_miss(const uint32_t *missb, int32_t K, int32_t cur)
 {
@@ -378,65 +392,164 @@ __device__ __forceinline__ int32_t next_miss(const uint32_t *missb, int32_t K, i
     return (w << 5) + __ffs(bits) - 1;
 }
 
-// Phase 2, one warp: replay the hand sweep over the hot slots. Returns false when the sweep
-// would pass a slot twice (the sequential path then takes the step).
+// Phase 2, one warp: replay the hand sweep over the hot slots, a batch of misses at a time.
+// Lane j of a window holds hot slot 32*w + j. A batch takes the next (up to) 32 queued misses
+// Q[0..nq) into lanes and assigns them to the window's slots in one go: slot j can be taken
+// by miss a only if Q[a] < Tf[j] (its token is not looked up before that miss), i.e. if
+// a < cap[j] = lower_bound(Q, Tf[j]); the greedy "each miss takes the next such slot" is
+// solved by assuming every candidate is taken and fixing the first slot that violates its
+// cap until none does. Evicting a slot whose token is looked up later creates the miss
+// Tf[j]; the batch is cut before the first miss later than the earliest created one, which
+// re-enters the queue. Slots passed are decided in registers and their final visited bits
+// written once per window. Only this warp runs during the phase. Returns false when the
+// sweep would pass a slot twice (the sequential path then takes the step).
 __device__ bool sweep_warp(const uint32_t *vini, uint32_t *vfin, const uint32_t *tf, uint16_t *evt,
                            uint32_t *missb, int32_t *os, int8_t *om, int32_t K, int32_t dbs, int32_t hand0,
-                           int32_t *hand_out)
+                           int32_t *hand_out, int32_t *qbuf)
 {
     const int lane = threadIdx.x & 31;
-    int32_t cur = next_miss(missb, K, -1);
-    int32_t cbase = hand0, passed0 = 0, pos = 0, last = -1;
-    int32_t c = 0;
-    bool valid = false;
+    const unsigned lt = (1u << lane) - 1u;
+    const int32_t nwords = (dbs + 31) >> 5;
+    const int32_t qwords = (K + 31) >> 5;
+    auto next_from = [&](int32_t n) -> int32_t {  // first queued miss >= n, K if none
+        if (n >= K) return K;
+        const int32_t w0 = n >> 5;
+        for (int32_t base = w0; base < qwords; base += 32) {
+            const int32_t wi = base + lane;
+            uint32_t b = wi < qwords ? missb[wi] : 0u;
+            if (wi == w0) b &= 0xFFFFFFFFu << (n & 31);
+            const unsigned nz = __ballot_sync(0xFFFFFFFFu, b != 0u);
+            if (nz) {
+                const int src = __ffs(nz) - 1;
+                const uint32_t bb = __shfl_sync(0xFFFFFFFFu, b, src);
+                return ((base + src) << 5) + __ffs(bb) - 1;
+            }
+        }
+        return K;
+    };
+    int32_t cur = next_from(0);
+    if (cur >= K) return true;  // no miss: hand unchanged
+
+    int32_t w = hand0 >> 5, pos = hand0 & 31, passed = 0, last = -1;
+    int32_t slot = 0;
+    bool real = false, decided = false, fbit = false;
     uint32_t ib = 1, tfv = kNone16, tlv = 0;
     auto load = [&]() {
-        c = cbase + lane;
-        while (c >= dbs) c -= dbs;
-        valid = passed0 + lane < dbs;
-        ib = valid ? (vini[c >> 5] >> (c & 31)) & 1u : 1u;
-        const uint32_t w = valid ? tf[c] : kNone16;
-        tfv = w & 0xFFFFu;
-        tlv = w >> 16;
+        slot = (w << 5) + lane;
+        real = slot < dbs;
+        ib = real ? (vini[w] >> lane) & 1u : 1u;
+        const uint32_t x = real ? tf[slot] : kNone16;
+        tfv = x & 0xFFFFu;
+        tlv = x >> 16;
+        decided = false;
+    };
+    auto retire = [&]() {  // publish the final bits of the slots passed in this visit
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, decided);
+        const unsigned b = __ballot_sync(0xFFFFFFFFu, decided && fbit);
+        if (lane == 0 && m) vfin[w] = (vfin[w] & ~m) | (b & m);
     };
     auto advance = [&]() {
-        passed0 += 32;
-        cbase += 32;
-        while (cbase >= dbs) cbase -= dbs;
+        retire();
+        w = (w + 1 == nwords) ? 0 : w + 1;
         pos = 0;
         load();
     };
     load();
-    bool ok = true;
     while (cur < K) {
-        const bool elig = valid && lane >= pos && ib == 0 && tfv > static_cast<uint32_t>(cur);
-        const unsigned E = __ballot_sync(0xFFFFFFFFu, elig);
-        if (E == 0) {
-            if (!__all_sync(0xFFFFFFFFu, valid)) {  // every remaining slot already passed: wrap
-                ok = false;
-                break;
+        // ---- the next queued misses Q[0..nq), one per lane (Q[0] = cur) ----
+        int32_t q, nq;
+        {
+            const int32_t w0 = cur >> 5;
+            const int32_t wi = w0 + lane;
+            uint32_t b = wi < qwords ? missb[wi] : 0u;
+            if (lane == 0) b &= 0xFFFFFFFFu << (cur & 31);
+            const int cnt = __popc(b);
+            int incl = cnt;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+                if (lane >= d) incl += v;
             }
-            if (lane >= pos) put_bit(vfin, c, tfv != kNone16 && tlv > static_cast<uint32_t>(cur));
+            int at = incl - cnt;
+            nq = min(__shfl_sync(0xFFFFFFFFu, incl, 31), 32);
+            while (b != 0u && at < 32) {
+                qbuf[at++] = (wi << 5) + __ffs(b) - 1;
+                b &= b - 1u;
+            }
+            __syncwarp();
+            q = lane < nq ? qbuf[lane] : K;
+            __syncwarp();
+        }
+        // ---- window slots that can still be passed; cap = lower_bound(Q, Tf) ----
+        const bool inrange = real && lane >= pos && passed + (lane - pos) < dbs;
+        const bool cand = inrange && ib == 0u;
+        int lo = 0, hi = nq;
+        for (int it = 0; it < 6; ++it) {
+            const int mid = (lo + hi) >> 1;
+            const int32_t qm = __shfl_sync(0xFFFFFFFFu, q, mid & 31);
+            if (lo < hi) {
+                if (static_cast<uint32_t>(qm) < tfv) lo = mid + 1;
+                else hi = mid;
+            }
+        }
+        const int cap = lo;
+        // ---- greedy assignment: take every candidate, then skip the first that violates its cap ----
+        unsigned S = 0u;
+        int f = pos, a = 0;
+        bool take = false;
+        for (int it = 0; it < 33; ++it) {
+            take = cand && !((S >> lane) & 1u);
+            a = __popc(__ballot_sync(0xFFFFFFFFu, take) & lt);
+            const unsigned viol = __ballot_sync(0xFFFFFFFFu, take && lane >= f && a < nq && cap <= a);
+            if (!viol) break;
+            const int js = __ffs(viol) - 1;
+            S |= 1u << js;
+            f = js + 1;
+        }
+        const bool evict = take && a < nq;
+        const unsigned em = __ballot_sync(0xFFFFFFFFu, evict);
+        if (em == 0u) {
+            // no slot of this window is free for `cur`: it passes them all
+            if (inrange) {
+                decided = true;
+                fbit = tfv != kNone16 && tlv > static_cast<uint32_t>(cur);
+            }
+            const int32_t npass = __popc(__ballot_sync(0xFFFFFFFFu, inrange));
+            const int32_t lanes_left = (w == nwords - 1 ? ((dbs - 1) & 31) + 1 : 32) - pos;
+            if (npass < lanes_left) return false;  // the passed-slot limit cut the window: wrap
+            passed += npass;
             advance();
             continue;
         }
-        const int j = __ffs(E) - 1;
-        if (lane >= pos && lane < j) put_bit(vfin, c, tfv != kNone16 && tlv > static_cast<uint32_t>(cur));
-        if (lane == j) {  // evict slot c at miss `cur`
-            os[cur] = c;
-            om[cur] = 1;
-            evt[c] = static_cast<uint16_t>(cur);
-            put_bit(vfin, c, true);
-            if (tfv != kNone16) atomicOr(&missb[tfv >> 5], 1u << (tfv & 31));  // its token's first lookup misses
+        // ---- cut the batch before the first miss later than the earliest created miss ----
+        const uint32_t Tmin = __reduce_min_sync(0xFFFFFFFFu, (evict && tfv != kNone16) ? tfv : 0xFFFFFFFFu);
+        const int32_t qa = __shfl_sync(0xFFFFFFFFu, q, a & 31);  // the miss reaching this slot
+        const bool commit = evict && static_cast<uint32_t>(qa) < Tmin;
+        const unsigned cm = __ballot_sync(0xFFFFFFFFu, commit);
+        const int lastlane = 31 - __clz(cm);
+        if (inrange && lane <= lastlane) {
+            decided = true;
+            if (commit) {  // evicted at miss qa
+                fbit = true;
+                os[qa] = slot;
+                om[qa] = 1;
+                evt[slot] = static_cast<uint16_t>(qa);
+                if (tfv != kNone16) atomicOr(&missb[tfv >> 5], 1u << (tfv & 31));  // its first lookup misses
+            } else {  // passed by miss qa: cleared, set again by a later hit
+                fbit = tfv != kNone16 && tlv > static_cast<uint32_t>(qa);
+            }
         }
-        last = __shfl_sync(0xFFFFFFFFu, c, j);
-        pos = j + 1;
-        if (pos == 32) advance();
+        const int32_t lastq = __shfl_sync(0xFFFFFFFFu, qa, lastlane);
+        last = (w << 5) + lastlane;
+        passed += lastlane - pos + 1;
+        pos = lastlane + 1;
+        const int32_t lane_end = (w == nwords - 1) ? ((dbs - 1) & 31) + 1 : 32;
+        if (pos >= lane_end) advance();
         __syncwarp();
-        cur = next_miss(missb, K, cur);
+        cur = next_from(lastq + 1);
     }
-    if (ok && last >= 0) *hand_out = last + 1 == dbs ? 0 : last + 1;
-    return ok;
+    retire();
+    *hand_out = last + 1 == dbs ? 0 : last + 1;
+    return true;
 }
 
 __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const SieveParams p)
@@ -447,6 +560,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     __shared__ int s_any_miss;
     __shared__ int32_t s_hand;
     __shared__ bool s_dirty;
+    __shared__ int32_t s_qbuf[32];
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -487,11 +601,11 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     const uint32_t dmask = static_cast<uint32_t>(L.dcap) - 1u;
 
     // ---- phase 0: stage the request's state, clear the step arrays ----
-    coop_copy(s_ht, g_ht, 2ull * p.ht_size);
-    coop_copy(s_tok, g_tok, 4ull * padded);
-    coop_copy(s_topk, g_topk, 4ull * K);
-    coop_copy(s_vini, g_vis, p.vis_stride);
-    coop_copy(s_vfin, g_vis, p.vis_stride);
+    stage_async(s_ht, g_ht, 2ull * p.ht_size);
+    stage_async(s_tok, g_tok, 4ull * padded);
+    stage_async(s_topk, g_topk, 4ull * K);
+    stage_async(s_vini, g_vis, p.vis_stride);
+    stage_async(s_vfin, g_vis, p.vis_stride);
     for (int32_t i = tid; i < dbs; i += nt) s_tf[i] = kNone16;  // Tf = none, Tl = 0
     for (int32_t i = tid; i < padded; i += nt) s_evt[i] = kNone16;
     for (int32_t i = tid; i < L.dcap; i += nt) {
@@ -507,6 +621,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
         s_any_miss = 0;
         s_changed[0] = s_changed[1] = 0;
     }
+    cp_async_wait_all();
     __syncthreads();
 
     // ---- phase 1: classify and probe every position against the step-initial table ----
@@ -572,7 +687,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     // ---- phase 2: the hand sweep, one warp ----
     if (!s_flag && tid < 32) {
         int32_t hand = s_hand;
-        const bool ok = sweep_warp(s_vini, s_vfin, s_tf, s_evt, s_missb, s_os, s_om, K, dbs, s_hand, &hand);
+        const bool ok = sweep_warp(s_vini, s_vfin, s_tf, s_evt, s_missb, s_os, s_om, K, dbs, s_hand, &hand, s_qbuf);
         if (tid == 0) {
             if (!ok) s_flag = 1;
             s_hand = hand;
