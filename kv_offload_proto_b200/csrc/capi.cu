@@ -246,6 +246,11 @@ int export_common(uint64_t seg_base, uint32_t plsr, uint32_t row_bytes, uint32_t
 
 }  // namespace
 
+namespace kvb {
+// Lets other translation units of this library report a failure through kvops_last_error().
+int set_last_error(int code, const char *msg) { return fail(code, msg); }
+}  // namespace kvb
+
 extern "C" {
 
 const char *kvops_last_error(void) { return g_last_error.c_str(); }

@@ -132,6 +132,9 @@ __device__ __forceinline__ void record_error(const StatusTarget &st, unsigned in
     if (st.ticket != nullptr) atomicCAS(&st.ticket->err, 0u, code);
 }
 
+// Records `msg` as the calling thread's last error (capi.cu) and returns `code`.
+int set_last_error(int code, const char *msg);
+
 // Kernel launchers (defined next to their kernels).
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int sm_count);
 cudaError_t launch_sieve_ht_init(const HtInitParams &p, cudaStream_t s);

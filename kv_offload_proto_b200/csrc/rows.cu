@@ -2,10 +2,10 @@
 // (kvc_scatter_rows_alllayer) for sm_100a.
 //
 // Both are sparse row copies bounded by HBM / NVLink / host-link bandwidth; no tensor
-// cores. A warp owns 32 candidate rows per iteration: lanes evaluate one position (or
-// destination row) each, the accepted rows are compacted with a ballot, and the warp
-// then streams them as one flat array of 16-byte chunks with 8 loads in flight per
-// lane before the matching stores. Sources may be own HBM, a peer GPU's HBM (UVA,
+// cores. A CTA owns a tile of 256 candidate rows per iteration: threads evaluate one
+// position (or destination row) each, the accepted rows are appended to a shared list, and
+// the whole CTA then streams the list as one flat array of 16-byte chunks with 8 loads in
+// flight per thread before the matching stores. Sources may be own HBM, a peer GPU's HBM (UVA,
 // NVLink/NVSwitch) or pinned host memory; loads are plain (no TMA, no multicast).
 #include <stdint.h>
 
@@ -15,7 +15,6 @@ namespace kvb {
 namespace {
 
 constexpr int kRowThreads = 256;
-constexpr int kRowWarps = kRowThreads / 32;
 constexpr int kUnroll = 8;
 
 template <typename V>
@@ -29,52 +28,55 @@ __device__ __forceinline__ uint8_t load_stream<uint8_t>(const uint8_t *p)
     return *reinterpret_cast<const volatile uint8_t *>(p);
 }
 
-// Copies n rows (src[i] -> dst[i], i < n, n <= 32) of `row_bytes` bytes with the whole warp.
+// Copies n rows (src[i] -> dst[i]) of `row_bytes` with the whole CTA: the rows form one flat
+// array of V-sized chunks split evenly over the threads, kUnroll loads in flight per thread
+// before the matching stores. `magic` = ceil(2^32 / chunks_per_row) when exact division by
+// multiply-high is valid for every chunk index (host-checked), else 0.
 template <typename V>
-__device__ __forceinline__ void warp_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
-                                               uint32_t row_bytes, int lane)
+__device__ __forceinline__ void cta_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
+                                              uint32_t row_bytes, uint32_t magic)
 {
-    const uint32_t cpr = row_bytes / sizeof(V);  // chunks per row
+    const uint32_t cpr = row_bytes / sizeof(V);
     const uint32_t total = static_cast<uint32_t>(n) * cpr;
-    // (r, c) = divmod(i, cpr) for i = lane, advanced by 32 per step without a division.
-    uint32_t r = 0, c = static_cast<uint32_t>(lane);
-    while (c >= cpr && r < static_cast<uint32_t>(n)) {
-        c -= cpr;
-        ++r;
-    }
-    for (uint32_t i0 = lane; i0 < total; i0 += 32u * kUnroll) {
+    for (uint32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * kUnroll) {
         V v[kUnroll];
         uint32_t rr[kUnroll], cc[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t i = i0 + u * blockDim.x;
+            const uint32_t r = magic ? __umulhi(i, magic) : i / cpr;
             rr[u] = r;
-            cc[u] = c;
-            if (i0 + 32u * u < total) v[u] = load_stream(reinterpret_cast<const V *>(src[r]) + c);
-            c += 32;
-            while (c >= cpr) {
-                c -= cpr;
-                ++r;
-            }
+            cc[u] = i - r * cpr;
+            if (i < total) v[u] = load_stream(reinterpret_cast<const V *>(src[r]) + cc[u]);
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            if (i0 + 32u * u < total) reinterpret_cast<V *>(dst[rr[u]])[cc[u]] = v[u];
+            if (i0 + u * blockDim.x < total) reinterpret_cast<V *>(dst[rr[u]])[cc[u]] = v[u];
         }
     }
 }
 
+// One tile = kGatherTile consecutive positions per CTA iteration: every thread evaluates one
+// position (kvc_gather_rows.cpp:54-76), the accepted rows are appended to a shared list, and
+// the CTA then copies the list with cta_copy_rows. The grid is sized to the GPU and loops over
+// tiles, so no wave is left partly empty.
+constexpr int kGatherTile = kRowThreads;
+
 template <typename V>
-__global__ void __launch_bounds__(kRowThreads) gather_kernel(const GatherParams p)
+__global__ void __launch_bounds__(kRowThreads, 4) gather_kernel(const GatherParams p, uint32_t magic)
 {
-    __shared__ const uint8_t *s_src[kRowWarps][32];
-    __shared__ uint8_t *s_dst[kRowWarps][32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ const uint8_t *s_src[kGatherTile];
+    __shared__ uint8_t *s_dst[kGatherTile];
+    __shared__ int s_n;
+    const int lane = threadIdx.x & 31;
     int32_t num_real = p.num_real != nullptr ? *p.num_real : 0;
     if (num_real > static_cast<int32_t>(p.max_num_reqs)) num_real = static_cast<int32_t>(p.max_num_reqs);
     const int64_t total = num_real > 0 ? static_cast<int64_t>(num_real) * p.top_k : 0;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * kRowWarps * 32;
-    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kRowWarps + warp) * 32; base < total; base += stride) {
-        const int64_t pos = base + lane;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kGatherTile; base < total;
+         base += static_cast<int64_t>(gridDim.x) * kGatherTile) {
+        if (threadIdx.x == 0) s_n = 0;
+        __syncthreads();
+        const int64_t pos = base + threadIdx.x;
         bool ok = false;
         const uint8_t *src = nullptr;
         uint8_t *dst = nullptr;
@@ -103,14 +105,16 @@ __global__ void __launch_bounds__(kRowThreads) gather_kernel(const GatherParams 
             }
         }
         const unsigned mask = __ballot_sync(0xFFFFFFFFu, ok);
+        int at = 0;
+        if (lane == 0 && mask) at = atomicAdd(&s_n, __popc(mask));
+        at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(mask & ((1u << lane) - 1u));
         if (ok) {
-            const int idx = __popc(mask & ((1u << lane) - 1u));
-            s_src[warp][idx] = src;
-            s_dst[warp][idx] = dst;
+            s_src[at] = src;
+            s_dst[at] = dst;
         }
-        __syncwarp();
-        if (mask) warp_copy_rows<V>(s_src[warp], s_dst[warp], __popc(mask), p.row_bytes, lane);
-        __syncwarp();
+        __syncthreads();
+        cta_copy_rows<V>(s_src, s_dst, s_n, p.row_bytes, magic);
+        __syncthreads();
     }
     __syncthreads();
     if (threadIdx.x == 0) arrive_and_publish(p.st);
@@ -145,16 +149,19 @@ __device__ __forceinline__ bool export_unit(const ExportParams &p, uint64_t k, u
 }
 
 template <typename V>
-__global__ void __launch_bounds__(kRowThreads) export_kernel(const ExportParams p)
+__global__ void __launch_bounds__(kRowThreads, 4) export_kernel(const ExportParams p, uint32_t magic)
 {
-    __shared__ const uint8_t *s_src[kRowWarps][32];
-    __shared__ uint8_t *s_dst[kRowWarps][32];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ const uint8_t *s_src[kGatherTile];
+    __shared__ uint8_t *s_dst[kGatherTile];
+    __shared__ int s_n;
+    const int lane = threadIdx.x & 31;
     const uint64_t total = p.units_per_layer * p.layer_num;
-    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kRowWarps * 32;
     if (p.seg_null && blockIdx.x == 0 && threadIdx.x == 0) record_error(p.st, KVOPS_ERR_SEG_NULL);
-    for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * kRowWarps + warp) * 32; base < total; base += stride) {
-        const uint64_t u = base + lane;
+    for (uint64_t base = static_cast<uint64_t>(blockIdx.x) * kGatherTile; base < total;
+         base += static_cast<uint64_t>(gridDim.x) * kGatherTile) {
+        if (threadIdx.x == 0) s_n = 0;
+        __syncthreads();
+        const uint64_t u = base + threadIdx.x;
         bool ok = false;
         const uint8_t *src = nullptr;
         uint8_t *dst = nullptr;
@@ -174,14 +181,16 @@ __global__ void __launch_bounds__(kRowThreads) export_kernel(const ExportParams 
             }
         }
         const unsigned mask = __ballot_sync(0xFFFFFFFFu, ok);
+        int at = 0;
+        if (lane == 0 && mask) at = atomicAdd(&s_n, __popc(mask));
+        at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(mask & ((1u << lane) - 1u));
         if (ok) {
-            const int idx = __popc(mask & ((1u << lane) - 1u));
-            s_src[warp][idx] = src;
-            s_dst[warp][idx] = dst;
+            s_src[at] = src;
+            s_dst[at] = dst;
         }
-        __syncwarp();
-        if (mask) warp_copy_rows<V>(s_src[warp], s_dst[warp], __popc(mask), p.row_bytes, lane);
-        __syncwarp();
+        __syncthreads();
+        cta_copy_rows<V>(s_src, s_dst, s_n, p.row_bytes, magic);
+        __syncthreads();
     }
     __syncthreads();
     if (threadIdx.x == 0) arrive_and_publish(p.st);
@@ -197,13 +206,6 @@ int vec_bytes(uint64_t addr_or, uint32_t row_bytes)
     return 1;
 }
 
-int grid_for(uint64_t work_warps, int sm_count)
-{
-    const uint64_t want = (work_warps + kRowWarps - 1) / kRowWarps;
-    const uint64_t cap = static_cast<uint64_t>(sm_count > 0 ? sm_count : 148) * (2048 / kRowThreads);
-    uint64_t g = want < cap ? want : cap;
-    return g < 1 ? 1 : static_cast<int>(g);
-}
 
 }  // namespace
 
@@ -213,12 +215,19 @@ cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count)
     for (uint32_t n = 0; n < p.nodes && n < static_cast<uint32_t>(kMaxNodes); ++n)
         addr_or |= reinterpret_cast<uint64_t>(p.seg[n]);
     const uint64_t positions = static_cast<uint64_t>(p.max_num_reqs) * p.top_k;
-    const int grid = grid_for((positions + 31) / 32, sm_count);
-    switch (vec_bytes(addr_or, p.row_bytes)) {
-        case 16: gather_kernel<uint4><<<grid, kRowThreads, 0, s>>>(p); break;
-        case 8: gather_kernel<uint2><<<grid, kRowThreads, 0, s>>>(p); break;
-        case 4: gather_kernel<uint32_t><<<grid, kRowThreads, 0, s>>>(p); break;
-        default: gather_kernel<uint8_t><<<grid, kRowThreads, 0, s>>>(p); break;
+    const uint64_t tiles = (positions + kGatherTile - 1) / kGatherTile;
+    const uint64_t cap = static_cast<uint64_t>(sm_count > 0 ? sm_count : 148) * 4;
+    const int grid = static_cast<int>(tiles < 1 ? 1 : (tiles < cap ? tiles : cap));
+    const int vb = vec_bytes(addr_or, p.row_bytes);
+    // chunk index < tile rows * chunks per row; exact multiply-high division needs i * e < 2^32
+    const uint64_t cpr = p.row_bytes / vb;
+    const uint32_t magic = (cpr > 0 && cpr < 65536 && kGatherTile * cpr < 65536)
+                               ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;
+    switch (vb) {
+        case 16: gather_kernel<uint4><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        case 8: gather_kernel<uint2><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        case 4: gather_kernel<uint32_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        default: gather_kernel<uint8_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
     }
     return cudaGetLastError();
 }
@@ -227,12 +236,18 @@ cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count)
 {
     const uint64_t addr_or = reinterpret_cast<uint64_t>(p.src0) | p.src_layer_stride | reinterpret_cast<uint64_t>(p.seg);
     const uint64_t units = p.units_per_layer * p.layer_num;
-    const int grid = grid_for((units + 31) / 32, sm_count);
-    switch (vec_bytes(addr_or, p.row_bytes)) {
-        case 16: export_kernel<uint4><<<grid, kRowThreads, 0, s>>>(p); break;
-        case 8: export_kernel<uint2><<<grid, kRowThreads, 0, s>>>(p); break;
-        case 4: export_kernel<uint32_t><<<grid, kRowThreads, 0, s>>>(p); break;
-        default: export_kernel<uint8_t><<<grid, kRowThreads, 0, s>>>(p); break;
+    const uint64_t tiles = (units + kGatherTile - 1) / kGatherTile;
+    const uint64_t cap = static_cast<uint64_t>(sm_count > 0 ? sm_count : 148) * 4;
+    const int grid = static_cast<int>(tiles < 1 ? 1 : (tiles < cap ? tiles : cap));
+    const int vb = vec_bytes(addr_or, p.row_bytes);
+    const uint64_t cpr = p.row_bytes / vb;
+    const uint32_t magic = (cpr > 0 && cpr < 65536 && kGatherTile * cpr < 65536)
+                               ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;
+    switch (vb) {
+        case 16: export_kernel<uint4><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        case 8: export_kernel<uint2><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        case 4: export_kernel<uint32_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        default: export_kernel<uint8_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
     }
     return cudaGetLastError();
 }

@@ -341,7 +341,7 @@ constexpr uint16_t kLeadMark = 0xFFFEu;  // table cell: first deleted entry of i
 constexpr uint8_t kClsNone = 0, kClsRes = 1, kClsNew = 2, kClsPending = 3, kClsPlaced = 4;
 
 struct FastLayout {
-    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, missb, total;
+    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, missb, wofs, total;
     int32_t dcap;
 };
 
@@ -370,186 +370,181 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
     L.evt = take(&o, 2ull * padded);
     L.vini = take(&o, static_cast<size_t>(vis_stride));
     L.vfin = take(&o, static_cast<size_t>(vis_stride));
-    L.dkey = take(&o, 4ull * L.dcap);
-    L.dfirst = take(&o, 4ull * L.dcap);
+    // The dedup table (phase 1) and the candidate list (phase 2) share one region.
+    const size_t dd = 8ull * L.dcap > 4ull * dbs + 16 ? 8ull * L.dcap : 4ull * dbs + 16;  // +16: whole 16-B chunks
+    L.dkey = take(&o, dd);
+    L.dfirst = L.dkey + 4ull * L.dcap;
     L.missb = take(&o, 4ull * ((K + 31) / 32));
+    L.wofs = take(&o, 4ull * ((dbs + 31) / 32 + 1));
     L.total = o;
     return L;
 }
 
-// Next queued miss position after `cur` (K if none).
-__device__ __forceinline__ int32_t next_miss(const uint32_t *missb, int32_t K, int32_t cur)
+
+// Phase 2 replays the hand sweep. Only slots whose visited bit is clear at the start of the
+// step can be evicted (a set bit is cleared and skipped; with no wrap the sweep never comes
+// back to it), so the walk runs over the compacted list of those candidate slots:
+//  2a. all threads build the list in slot order, entries (Tf << 16) | slot;
+//  2b. one thread walks it from the hand: the current miss evicts the next candidate whose
+//      token is not looked up before it (Tf > miss); an evicted slot whose token is looked up
+//      later queues that lookup as a miss. Each visited entry is overwritten with its
+//      arrival time (the miss in progress when the sweep reaches it);
+//  2c. all threads set the final visited bits of the passed slots: evicted ones are set, the
+//      others were cleared on arrival and are set again iff their token is looked up after
+//      it. A passed slot's arrival time is that of the next candidate at or after it.
+
+// 2a: candidate list and per-word offsets; returns the candidate count (in *n_out).
+__device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint32_t *cand, uint32_t *wofs,
+                                 int32_t dbs, int32_t *n_out, int32_t *warp_sums)
 {
-    const int32_t n = cur + 1;
-    if (n >= K) return K;
-    const int32_t nw = (K + 31) >> 5;
-    int32_t w = n >> 5;
-    uint32_t bits = missb[w] & (0xFFFFFFFFu << (n & 31));
-    while (bits == 0) {
-        if (++w >= nw) return K;
-        bits = missb[w];
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+    const int32_t nwords = (dbs + 31) >> 5;
+    const int32_t per = (nwords + nt - 1) / nt;
+    const int32_t w0 = min(tid * per, nwords), w1 = min(w0 + per, nwords);
+    auto bits_of = [&](int32_t w) -> uint32_t {
+        const int32_t rem = dbs - (w << 5);
+        const uint32_t valid = rem >= 32 ? 0xFFFFFFFFu : ((1u << rem) - 1u);
+        return ~vini[w] & valid;
+    };
+    int32_t mine = 0;
+    for (int32_t w = w0; w < w1; ++w) mine += __popc(bits_of(w));
+    // block-wide exclusive scan of `mine`
+    int32_t incl = mine;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
     }
-    return (w << 5) + __ffs(bits) - 1;
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = nt >> 5;
+        int32_t v = lane < nw ? warp_sums[lane] : 0, inc = v;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int32_t u = __shfl_up_sync(0xFFFFFFFFu, inc, d);
+            if (lane >= d) inc += u;
+        }
+        if (lane < nw) warp_sums[lane] = inc - v;  // exclusive warp offsets
+        if (lane == nw - 1) *n_out = inc;
+    }
+    __syncthreads();
+    int32_t at = warp_sums[wid] + incl - mine;
+    for (int32_t w = w0; w < w1; ++w) {
+        wofs[w] = static_cast<uint32_t>(at);
+        uint32_t b = bits_of(w);
+        while (b) {
+            const int32_t c = (w << 5) + __ffs(b) - 1;
+            b &= b - 1u;
+            cand[at++] = ((tf[c] & 0xFFFFu) << 16) | static_cast<uint32_t>(c);
+        }
+    }
 }
 
-// Phase 2, one warp: replay the hand sweep over the hot slots, a batch of misses at a time.
-// Lane j of a window holds hot slot 32*w + j. A batch takes the next (up to) 32 queued misses
-// Q[0..nq) into lanes and assigns them to the window's slots in one go: slot j can be taken
-// by miss a only if Q[a] < Tf[j] (its token is not looked up before that miss), i.e. if
-// a < cap[j] = lower_bound(Q, Tf[j]); the greedy "each miss takes the next such slot" is
-// solved by assuming every candidate is taken and fixing the first slot that violates its
-// cap until none does. Evicting a slot whose token is looked up later creates the miss
-// Tf[j]; the batch is cut before the first miss later than the earliest created one, which
-// re-enters the queue. Slots passed are decided in registers and their final visited bits
-// written once per window. Only this warp runs during the phase. Returns false when the
-// sweep would pass a slot twice (the sequential path then takes the step).
-__device__ bool sweep_warp(const uint32_t *vini, uint32_t *vfin, const uint32_t *tf, uint16_t *evt,
-                           uint32_t *missb, int32_t *os, int8_t *om, int32_t K, int32_t dbs, int32_t hand0,
-                           int32_t *hand_out, int32_t *qbuf)
+// 2b: the walk (one thread). Candidates are read four at a time from a 16-byte load issued
+// one chunk ahead and handled with predicated code: t = 0xFFFF once the queue is empty, so
+// no candidate compares above it. The miss queue's current and next words live in
+// registers (created misses also go to the shared queue with a non-returning atomic).
+// Returns false when the sweep would pass a slot twice.
+__device__ __forceinline__ void walk_one(uint32_t &xv, uint32_t &t, int32_t &qw, uint32_t &cw, uint32_t &cwn,
+                                         int32_t &last, uint16_t *evt, uint32_t *missb, int32_t *os, int8_t *om,
+                                         int32_t qwords)
 {
-    const int lane = threadIdx.x & 31;
-    const unsigned lt = (1u << lane) - 1u;
-    const int32_t nwords = (dbs + 31) >> 5;
-    const int32_t qwords = (K + 31) >> 5;
-    auto next_from = [&](int32_t n) -> int32_t {  // first queued miss >= n, K if none
-        if (n >= K) return K;
-        const int32_t w0 = n >> 5;
-        for (int32_t base = w0; base < qwords; base += 32) {
-            const int32_t wi = base + lane;
-            uint32_t b = wi < qwords ? missb[wi] : 0u;
-            if (wi == w0) b &= 0xFFFFFFFFu << (n & 31);
-            const unsigned nz = __ballot_sync(0xFFFFFFFFu, b != 0u);
-            if (nz) {
-                const int src = __ffs(nz) - 1;
-                const uint32_t bb = __shfl_sync(0xFFFFFFFFu, b, src);
-                return ((base + src) << 5) + __ffs(bb) - 1;
-            }
+    const uint32_t tfv = xv >> 16, slot = xv & 0xFFFFu;
+    xv = (t << 16) | slot;  // arrival time of this candidate
+    if (tfv > t) {          // evict `slot` at miss t (never when t == 0xFFFF)
+        os[t] = static_cast<int32_t>(slot);
+        om[t] = 1;
+        evt[slot] = static_cast<uint16_t>(t);
+        last = static_cast<int32_t>(slot);
+        if (tfv != kNone16) {  // its token's first lookup (tfv > t) becomes a miss
+            const int32_t wt = static_cast<int32_t>(tfv >> 5);
+            const uint32_t bt = 1u << (tfv & 31);
+            atomicOr(&missb[wt], bt);
+            cw |= wt == qw ? bt : 0u;
+            cwn |= wt == qw + 1 ? bt : 0u;
         }
-        return K;
-    };
-    int32_t cur = next_from(0);
-    if (cur >= K) return true;  // no miss: hand unchanged
-
-    int32_t w = hand0 >> 5, pos = hand0 & 31, passed = 0, last = -1;
-    int32_t slot = 0;
-    bool real = false, decided = false, fbit = false;
-    uint32_t ib = 1, tfv = kNone16, tlv = 0;
-    auto load = [&]() {
-        slot = (w << 5) + lane;
-        real = slot < dbs;
-        ib = real ? (vini[w] >> lane) & 1u : 1u;
-        const uint32_t x = real ? tf[slot] : kNone16;
-        tfv = x & 0xFFFFu;
-        tlv = x >> 16;
-        decided = false;
-    };
-    auto retire = [&]() {  // publish the final bits of the slots passed in this visit
-        const unsigned m = __ballot_sync(0xFFFFFFFFu, decided);
-        const unsigned b = __ballot_sync(0xFFFFFFFFu, decided && fbit);
-        if (lane == 0 && m) vfin[w] = (vfin[w] & ~m) | (b & m);
-    };
-    auto advance = [&]() {
-        retire();
-        w = (w + 1 == nwords) ? 0 : w + 1;
-        pos = 0;
-        load();
-    };
-    load();
-    while (cur < K) {
-        // ---- the next queued misses Q[0..nq), one per lane (Q[0] = cur) ----
-        int32_t q, nq;
-        {
-            const int32_t w0 = cur >> 5;
-            const int32_t wi = w0 + lane;
-            uint32_t b = wi < qwords ? missb[wi] : 0u;
-            if (lane == 0) b &= 0xFFFFFFFFu << (cur & 31);
-            const int cnt = __popc(b);
-            int incl = cnt;
-            for (int d = 1; d < 32; d <<= 1) {
-                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
-                if (lane >= d) incl += v;
-            }
-            int at = incl - cnt;
-            nq = min(__shfl_sync(0xFFFFFFFFu, incl, 31), 32);
-            while (b != 0u && at < 32) {
-                qbuf[at++] = (wi << 5) + __ffs(b) - 1;
-                b &= b - 1u;
-            }
-            __syncwarp();
-            q = lane < nq ? qbuf[lane] : K;
-            __syncwarp();
+        cw &= ~(1u << (t & 31));
+        while (cw == 0u && qw < qwords) {
+            ++qw;
+            cw = cwn;
+            cwn = qw + 1 < qwords ? missb[qw + 1] : 0u;
         }
-        // ---- window slots that can still be passed; cap = lower_bound(Q, Tf) ----
-        const bool inrange = real && lane >= pos && passed + (lane - pos) < dbs;
-        const bool cand = inrange && ib == 0u;
-        int lo = 0, hi = nq;
-        for (int it = 0; it < 6; ++it) {
-            const int mid = (lo + hi) >> 1;
-            const int32_t qm = __shfl_sync(0xFFFFFFFFu, q, mid & 31);
-            if (lo < hi) {
-                if (static_cast<uint32_t>(qm) < tfv) lo = mid + 1;
-                else hi = mid;
-            }
-        }
-        const int cap = lo;
-        // ---- greedy assignment: take every candidate, then skip the first that violates its cap ----
-        unsigned S = 0u;
-        int f = pos, a = 0;
-        bool take = false;
-        for (int it = 0; it < 33; ++it) {
-            take = cand && !((S >> lane) & 1u);
-            a = __popc(__ballot_sync(0xFFFFFFFFu, take) & lt);
-            const unsigned viol = __ballot_sync(0xFFFFFFFFu, take && lane >= f && a < nq && cap <= a);
-            if (!viol) break;
-            const int js = __ffs(viol) - 1;
-            S |= 1u << js;
-            f = js + 1;
-        }
-        const bool evict = take && a < nq;
-        const unsigned em = __ballot_sync(0xFFFFFFFFu, evict);
-        if (em == 0u) {
-            // no slot of this window is free for `cur`: it passes them all
-            if (inrange) {
-                decided = true;
-                fbit = tfv != kNone16 && tlv > static_cast<uint32_t>(cur);
-            }
-            const int32_t npass = __popc(__ballot_sync(0xFFFFFFFFu, inrange));
-            const int32_t lanes_left = (w == nwords - 1 ? ((dbs - 1) & 31) + 1 : 32) - pos;
-            if (npass < lanes_left) return false;  // the passed-slot limit cut the window: wrap
-            passed += npass;
-            advance();
-            continue;
-        }
-        // ---- cut the batch before the first miss later than the earliest created miss ----
-        const uint32_t Tmin = __reduce_min_sync(0xFFFFFFFFu, (evict && tfv != kNone16) ? tfv : 0xFFFFFFFFu);
-        const int32_t qa = __shfl_sync(0xFFFFFFFFu, q, a & 31);  // the miss reaching this slot
-        const bool commit = evict && static_cast<uint32_t>(qa) < Tmin;
-        const unsigned cm = __ballot_sync(0xFFFFFFFFu, commit);
-        const int lastlane = 31 - __clz(cm);
-        if (inrange && lane <= lastlane) {
-            decided = true;
-            if (commit) {  // evicted at miss qa
-                fbit = true;
-                os[qa] = slot;
-                om[qa] = 1;
-                evt[slot] = static_cast<uint16_t>(qa);
-                if (tfv != kNone16) atomicOr(&missb[tfv >> 5], 1u << (tfv & 31));  // its first lookup misses
-            } else {  // passed by miss qa: cleared, set again by a later hit
-                fbit = tfv != kNone16 && tlv > static_cast<uint32_t>(qa);
-            }
-        }
-        const int32_t lastq = __shfl_sync(0xFFFFFFFFu, qa, lastlane);
-        last = (w << 5) + lastlane;
-        passed += lastlane - pos + 1;
-        pos = lastlane + 1;
-        const int32_t lane_end = (w == nwords - 1) ? ((dbs - 1) & 31) + 1 : 32;
-        if (pos >= lane_end) advance();
-        __syncwarp();
-        cur = next_from(lastq + 1);
+        t = cw ? static_cast<uint32_t>((qw << 5) + __ffs(cw) - 1) : 0xFFFFu;
     }
-    retire();
-    *hand_out = last + 1 == dbs ? 0 : last + 1;
+}
+
+__device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t *evt, uint32_t *missb,
+                                int32_t *os, int8_t *om, int32_t K, int32_t *last_out)
+{
+    const int32_t qwords = (K + 31) >> 5;
+    int32_t qw = 0;
+    uint32_t cw = missb[0];
+    uint32_t cwn = qwords > 1 ? missb[1] : 0u;
+    while (cw == 0u && qw < qwords) {
+        ++qw;
+        cw = cwn;
+        cwn = qw + 1 < qwords ? missb[qw + 1] : 0u;
+    }
+    uint32_t t = cw ? static_cast<uint32_t>((qw << 5) + __ffs(cw) - 1) : 0xFFFFu;
+    int32_t last = -1;
+    for (int sg = 0; sg < 2 && t != 0xFFFFu; ++sg) {  // [n0, n) then, wrapping, [0, n0)
+        int32_t i = sg == 0 ? n0 : 0;
+        const int32_t hi = sg == 0 ? n : n0;
+        // head: up to 3 entries before the first 16-byte boundary
+        for (; i < hi && (i & 3) != 0 && t != 0xFFFFu; ++i)
+            walk_one(cand[i], t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+        // body: whole chunks, the next one loaded ahead
+        if (i + 4 <= hi && t != 0xFFFFu) {
+            uint4 vn = *reinterpret_cast<const uint4 *>(cand + i);
+            while (i + 4 <= hi && t != 0xFFFFu) {
+                uint4 v = vn;
+                if (i + 8 <= hi) vn = *reinterpret_cast<const uint4 *>(cand + i + 4);
+                walk_one(v.x, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+                walk_one(v.y, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+                walk_one(v.z, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+                walk_one(v.w, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+                *reinterpret_cast<uint4 *>(cand + i) = v;
+                i += 4;
+            }
+        }
+        // tail
+        for (; i < hi && t != 0xFFFFu; ++i) walk_one(cand[i], t, qw, cw, cwn, last, evt, missb, os, om, qwords);
+    }
+    if (t != 0xFFFFu) return false;  // every candidate passed once: the sweep would wrap
+    *last_out = last;
     return true;
+}
+
+// 2c: final visited bits of the slots passed, one word per thread.
+__device__ void passed_bits(const uint32_t *vini, uint32_t *vfin, const uint32_t *tf, const uint16_t *evt,
+                            const uint32_t *cand, const uint32_t *wofs, int32_t n, int32_t dbs, int32_t hand0,
+                            int32_t last)
+{
+    const int32_t nwords = (dbs + 31) >> 5;
+    const int32_t pend = (last - hand0 + dbs) % dbs + 1;  // slots passed, in sweep order from the hand
+    for (int32_t w = threadIdx.x; w < nwords; w += blockDim.x) {
+        uint32_t m = 0u, b = 0u;
+        int32_t q = static_cast<int32_t>(wofs[w]);  // candidates before this slot, slot order
+        const uint32_t ini = vini[w];
+        for (int l = 0; l < 32; ++l) {
+            const int32_t c = (w << 5) + l;
+            if (c >= dbs) break;
+            const bool is_cand = ((ini >> l) & 1u) == 0u;
+            int32_t pos = c - hand0;
+            if (pos < 0) pos += dbs;
+            if (pos < pend) {
+                m |= 1u << l;
+                if (evt[c] != kNone16) {
+                    b |= 1u << l;
+                } else {
+                    const uint32_t arr = cand[q == n ? 0 : q] >> 16;  // next candidate at or after c
+                    const uint32_t x = tf[c];
+                    if ((x & 0xFFFFu) != kNone16 && (x >> 16) > arr) b |= 1u << l;
+                }
+            }
+            if (is_cand) ++q;
+        }
+        if (m) vfin[w] = (vfin[w] & ~m) | (b & m);
+    }
 }
 
 __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const SieveParams p)
@@ -560,7 +555,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     __shared__ int s_any_miss;
     __shared__ int32_t s_hand;
     __shared__ bool s_dirty;
-    __shared__ int32_t s_qbuf[32];
+    __shared__ int32_t s_warp[32];
+    __shared__ int32_t s_ncand, s_last, s_nkeys;
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -684,15 +680,27 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     }
     __syncthreads();
 
-    // ---- phase 2: the hand sweep, one warp ----
-    if (!s_flag && tid < 32) {
-        int32_t hand = s_hand;
-        const bool ok = sweep_warp(s_vini, s_vfin, s_tf, s_evt, s_missb, s_os, s_om, K, dbs, s_hand, &hand, s_qbuf);
-        if (tid == 0) {
-            if (!ok) s_flag = 1;
-            s_hand = hand;
-            s_any_miss = next_miss(s_missb, K, -1) < K;
-        }
+    // ---- phase 2: the hand sweep (candidate list, one-thread walk, final bits) ----
+    uint32_t *s_cand = reinterpret_cast<uint32_t *>(smem + L.dkey);  // dedup table no longer needed
+    uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
+    if (!s_flag) build_candidates(s_vini, s_tf, s_cand, s_wofs, dbs, &s_ncand, s_warp);
+    __syncthreads();
+    if (!s_flag && tid == 0) {
+        const int32_t n = s_ncand;
+        const int32_t h0 = s_hand;
+        // first candidate at or after the hand, in slot order
+        int32_t n0 = static_cast<int32_t>(s_wofs[h0 >> 5]) +
+                     __popc(~s_vini[h0 >> 5] & ((1u << (h0 & 31)) - 1u));
+        if (n0 >= n) n0 = 0;
+        int32_t last = -1;
+        if (!walk_candidates(s_cand, n, n0, s_evt, s_missb, s_os, s_om, K, &last)) s_flag = 1;
+        s_last = last;
+        s_any_miss = last >= 0;
+    }
+    __syncthreads();
+    if (!s_flag && s_last >= 0) {
+        passed_bits(s_vini, s_vfin, s_tf, s_evt, s_cand, s_wofs, s_ncand, dbs, s_hand, s_last);
+        if (tid == 0) s_hand = s_last + 1 == dbs ? 0 : s_last + 1;
     }
     __syncthreads();
 
@@ -804,24 +812,34 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     __syncthreads();
 
     // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
+    uint16_t *s_keys = reinterpret_cast<uint16_t *>(smem + L.dkey);  // candidate list no longer needed
     if (update_table) {
-        for (int32_t m = tid; m < K; m += nt) {
-            if ((s_missb[m >> 5] >> (m & 31)) & 1u) {
+        if (tid == 0) s_nkeys = 0;
+        __syncthreads();
+        for (int32_t m0 = 0; m0 < K; m0 += nt) {  // list the misses (warp-aggregated appends)
+            const int32_t m = m0 + tid;
+            const bool is_key = m < K && ((s_missb[m >> 5] >> (m & 31)) & 1u);
+            const unsigned bal = __ballot_sync(0xFFFFFFFFu, is_key);
+            int at = 0;
+            if ((tid & 31) == 0 && bal) at = atomicAdd(&s_nkeys, __popc(bal));
+            at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(bal & ((1u << (tid & 31)) - 1u));
+            if (is_key) {
+                s_keys[at] = static_cast<uint16_t>(m);
                 s_aux[m] = static_cast<uint16_t>(ht_hash(s_topk[m]) & mask);
                 s_cls[m] = kClsPending;
-            } else {
-                s_cls[m] = kClsNone;
             }
         }
     }
     __syncthreads();
     if (update_table) {
+        const int32_t nkeys = s_nkeys;
         const int32_t limit = 4 * p.ht_size + 64;
         for (int32_t round = 0;; ++round) {
             // Round r raises s_changed[r & 1]; thread 0 clears the other flag once every thread
             // has passed the first barrier of round r, i.e. after all reads of round r-1's flag.
             bool ch = false;
-            for (int32_t m = tid; m < K; m += nt) {
+            for (int32_t j = tid; j < nkeys; j += nt) {
+                const int32_t m = s_keys[j];
                 if (s_cls[m] != kClsPending) continue;
                 const uint16_t entry = static_cast<uint16_t>(s_os[m] + 1);
                 const uint32_t at = s_aux[m];
@@ -842,7 +860,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             }
             __syncthreads();
             if (tid == 0) s_changed[(round + 1) & 1] = 0;
-            for (int32_t m = tid; m < K; m += nt) {
+            for (int32_t j = tid; j < nkeys; j += nt) {
+                const int32_t m = s_keys[j];
                 if (s_cls[m] == kClsPlaced && s_ht[s_aux[m]] != static_cast<uint16_t>(s_os[m] + 1)) {
                     s_cls[m] = kClsPending;
                     s_aux[m] = static_cast<uint16_t>((s_aux[m] + 1) & mask);
