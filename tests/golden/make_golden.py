@@ -1,8 +1,8 @@
 """Generate the golden fixtures under tests/golden/ from the reference's own Python code.
 
-Run in a container where the reference tree is mounted (default /root/reference):
+Run where the reference tree is mounted (its root is given with --ref):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference root>]
 
 It imports, read-only and unmodified:
   * xds.xds_decode._CpuSieveOracle   (xds/xds_decode.py:66-118)  — the SIEVE oracle
