@@ -12,7 +12,8 @@
  * Launches are asynchronous on `stream`; device-side failures are reported as
  * errCode values in the 64-byte status slot, as in the reference.
  *
- * Status slot layout (one self-consistent choice): a launch for
+ * Status slot layout (one self-consistent choice among the reference's conflicting
+ * writers and pollers, kvc_gather_rows.cpp:22-23 vs xds_ems_pool.py:238): a launch for
  * segment `my_node` with `block_dim` = B writes B 64-bit words at
  * status + my_node*64 + b*8 (b < B), each equal to (1 << 32) | errCode once every
  * row of the launch has landed. That is exactly what EmsPool.wait polls
@@ -149,6 +150,23 @@ int kvops_sieve_ht_init(uint64_t device_buffer_tokens, uint64_t device_buffer_ht
                         uint32_t req_start, uint32_t num_reqs, uint32_t layer_num, uint32_t pool_size,
                         uint32_t device_buffer_size, uint32_t padded_buffer_size, uint32_t ht_size,
                         uint64_t stream, uint32_t block_dim);
+
+/* No counterpart in the reference. kvops_import_multi for callers that cannot allocate
+ * device memory (an engine whose HBM is owned by its own allocator or fixed budget, or a
+ * decode loop that cannot pay for cudaMalloc/cudaFree): it calls no allocating routine.
+ * Its only scratch, the launch's 8-byte completion ticket, lives in a static device array
+ * of KVOPS_NOALLOC_SCRATCH_BYTES bytes held by every GPU that loads the library until exit.
+ * All calls share that array (cleared on `stream` before each launch), so calls whose
+ * launches overlap on the GPU race and must not be issued. The first call on a device looks
+ * up the array's device address; make it before any stream capture. Launches that would
+ * need more scratch than the array holds are rejected with KVOPS_E_INVALID. */
+#define KVOPS_NOALLOC_SCRATCH_BYTES 256
+int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg_bases, uint32_t layer_offset_rows,
+                               uint32_t per_layer_seg_rows, uint32_t row_bytes, uint64_t topk_indices,
+                               uint64_t req_pool_indices, uint64_t req_host_base, uint64_t topk_device_slots,
+                               uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base, uint32_t top_k,
+                               uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
+                               uint32_t block_dim, const KvopsRowOpts *opts);
 
 /* Pool plumbing that replaces the EMS control plane (not a reference entry point):
  * segment memory on a device (or pinned host memory with device = -1), peer access,

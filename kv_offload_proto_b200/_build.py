@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libkvops_b200.so")
 EXT = os.path.join(PKG, "kvops_ext", "_kvops" + sysconfig.get_config_var("EXT_SUFFIX"))
-CU_SOURCES = ["capi.cu", "sieve.cu", "rows.cu"]
+CU_SOURCES = ["capi.cu", "sieve.cu", "rows.cu", "noalloc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
