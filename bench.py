@@ -123,37 +123,26 @@ def state_bytes(padded, vis, ht_size):
 
 
 def build_pool(mod, torch, dist, rank, world, local, L, layer_rows, seed):
-    """Segments of this rank's pool. N=1: one segment in own HBM. N>1: node i of rank h's pool
-    lives on the i-th GPU other than h; every rank allocates and fills the segments it hosts
-    and maps its own pool's segments from the other ranks through CUDA IPC handles."""
+    """Segments of this rank's pool (kv_offload_proto_b200.cluster): every rank allocates and
+    fills the segments it hosts and maps its own pool's segments through CUDA IPC handles."""
+    from kv_offload_proto_b200.cluster import exchange_handles, hosted_segments, pool_nodes
     from kv_offload_proto_b200.pool import device_view, per_layer_seg_rows
-    nodes_of = (lambda h: [h]) if world == 1 else (lambda h: [g for g in range(world) if g != h])
-    n = len(nodes_of(rank))
-    seg_bytes = L * per_layer_seg_rows(layer_rows, n) * ROW_BYTES
+    nodes = pool_nodes(rank, world)
+    seg_bytes = L * per_layer_seg_rows(layer_rows, len(nodes)) * ROW_BYTES
     hosted = {}
-    for h in range(world):
-        if world > 1 and h == rank:
-            continue
-        idx = nodes_of(h).index(rank)
+    for owner, idx in hosted_segments(rank, world):
         addr = mod.segment_alloc(local, seg_bytes)
         view = device_view(addr, seg_bytes, "cuda:{}".format(local)).view(torch.float16)
-        gen = torch.Generator(device="cuda:{}".format(local)).manual_seed(seed * 7919 + h * 131 + idx)
+        gen = torch.Generator(device="cuda:{}".format(local)).manual_seed(seed * 7919 + owner * 131 + idx)
         chunk = 1 << 29
         for o in range(0, view.numel(), chunk):
             view[o:o + chunk].normal_(generator=gen)
-        hosted[(h, idx)] = addr
+        hosted[(owner, idx)] = addr
     if world == 1:
-        return [hosted[(rank, 0)]], nodes_of(rank), list(hosted.values()), []
-    handles = {k: mod.ipc_get_handle(a) for k, a in hosted.items()}
-    everyone = [None] * world
-    dist.all_gather_object(everyone, handles)
-    mine = [None] * n
-    for hd in everyone:
-        for (h, idx), hnd in hd.items():
-            if h == rank:
-                mine[idx] = mod.ipc_open_handle(local, hnd)
-    assert all(a is not None for a in mine)
-    return mine, nodes_of(rank), list(hosted.values()), list(mine)
+        return [hosted[(rank, 0)]], nodes, list(hosted.values()), []
+    handles = exchange_handles(dist, rank, world, {k: mod.ipc_get_handle(a) for k, a in hosted.items()})
+    mine = [mod.ipc_open_handle(local, h) for h in handles]
+    return mine, nodes, list(hosted.values()), list(mine)
 
 
 def run_b200(args):
