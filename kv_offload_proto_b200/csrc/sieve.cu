@@ -385,7 +385,7 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
 // step can be evicted (a set bit is cleared and skipped; with no wrap the sweep never comes
 // back to it), so the walk runs over the compacted list of those candidate slots:
 //  2a. all threads build the list in slot order, entries (Tf << 16) | slot;
-//  2b. one thread walks it from the hand: the current miss evicts the next candidate whose
+//  2b. one warp walks it from the hand: the current miss evicts the next candidate whose
 //      token is not looked up before it (Tf > miss); an evicted slot whose token is looked up
 //      later queues that lookup as a miss. Each visited entry is overwritten with its
 //      arrival time (the miss in progress when the sweep reaches it);
@@ -439,77 +439,150 @@ __device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint3
     }
 }
 
-// 2b: the walk (one thread). Candidates are read four at a time from a 16-byte load issued
-// one chunk ahead and handled with predicated code: t = 0xFFFF once the queue is empty, so
-// no candidate compares above it. The miss queue's current and next words live in
-// registers (created misses also go to the shared queue with a non-returning atomic).
-// Returns false when the sweep would pass a slot twice.
-__device__ __forceinline__ void walk_one(uint32_t &xv, uint32_t &t, int32_t &qw, uint32_t &cw, uint32_t &cwn,
-                                         int32_t &last, uint16_t *evt, uint32_t *missb, int32_t *os, int8_t *om,
-                                         int32_t qwords)
+// Position of the n-th (from 0) set bit of v, by halving; n < popc(v) gives a set bit, any
+// other n some position in [0, 31].
+__device__ __forceinline__ int select_bit(uint32_t v, int32_t n)
 {
-    const uint32_t tfv = xv >> 16, slot = xv & 0xFFFFu;
-    xv = (t << 16) | slot;  // arrival time of this candidate
-    if (tfv > t) {          // evict `slot` at miss t (never when t == 0xFFFF)
-        os[t] = static_cast<int32_t>(slot);
-        om[t] = 1;
-        evt[slot] = static_cast<uint16_t>(t);
-        last = static_cast<int32_t>(slot);
-        if (tfv != kNone16) {  // its token's first lookup (tfv > t) becomes a miss
-            const int32_t wt = static_cast<int32_t>(tfv >> 5);
-            const uint32_t bt = 1u << (tfv & 31);
-            atomicOr(&missb[wt], bt);
-            cw |= wt == qw ? bt : 0u;
-            cwn |= wt == qw + 1 ? bt : 0u;
+    int pos = 0;
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+        const int32_t c = __popc(v & ((1u << width) - 1u));
+        if (c <= n) {
+            n -= c;
+            v >>= width;
+            pos += width;
         }
-        cw &= ~(1u << (t & 31));
-        while (cw == 0u && qw < qwords) {
-            ++qw;
-            cw = cwn;
-            cwn = qw + 1 < qwords ? missb[qw + 1] : 0u;
-        }
-        t = cw ? static_cast<uint32_t>((qw << 5) + __ffs(cw) - 1) : 0xFFFFu;
     }
+    return pos;
 }
 
+// 2b: the walk (one warp), 32 candidates per batch, one per lane, in sweep order from the
+// hand. One round resolves many candidates at once:
+//  - the window: the next (up to) 32 queued misses at or after tq (32 queue words);
+//  - each lane ranks its token's first lookup Tf among them: t_j = misses in the window
+//    before Tf (a lookup before tq ranks 0; none, or one past the window, ranks all);
+//  - the sweep with this queue is the recurrence k <- k + (k < t_j) over the lanes: the
+//    lane is reached by the window's miss number k and evicted iff k < t_j;
+//  - an evicted lane whose token is looked up later creates the miss Tf, which this queue
+//    lacks. Every lane reached before the earliest such Tf (cmin) is exact, since the queue
+//    is exact below cmin; those lanes, always at least the first one, are committed and the
+//    created misses join the shared queue. The next round starts after the last eviction.
+// Each round commits a lane or moves the window past 1024 empty positions, which bounds the
+// rounds. Returns false when the sweep would pass a slot twice (misses remain after every
+// candidate), or if the bound were ever exceeded.
 __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t *evt, uint32_t *missb,
                                 int32_t *os, int8_t *om, int32_t K, int32_t *last_out)
 {
+    const unsigned kAll = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
     const int32_t qwords = (K + 31) >> 5;
-    int32_t qw = 0;
-    uint32_t cw = missb[0];
-    uint32_t cwn = qwords > 1 ? missb[1] : 0u;
-    while (cw == 0u && qw < qwords) {
-        ++qw;
-        cw = cwn;
-        cwn = qw + 1 < qwords ? missb[qw + 1] : 0u;
-    }
-    uint32_t t = cw ? static_cast<uint32_t>((qw << 5) + __ffs(cw) - 1) : 0xFFFFu;
+    int32_t tq = 0;  // first position the sweep has not consumed
     int32_t last = -1;
-    for (int sg = 0; sg < 2 && t != 0xFFFFu; ++sg) {  // [n0, n) then, wrapping, [0, n0)
-        int32_t i = sg == 0 ? n0 : 0;
-        const int32_t hi = sg == 0 ? n : n0;
-        // head: up to 3 entries before the first 16-byte boundary
-        for (; i < hi && (i & 3) != 0 && t != 0xFFFFu; ++i)
-            walk_one(cand[i], t, qw, cw, cwn, last, evt, missb, os, om, qwords);
-        // body: whole chunks, the next one loaded ahead
-        if (i + 4 <= hi && t != 0xFFFFu) {
-            uint4 vn = *reinterpret_cast<const uint4 *>(cand + i);
-            while (i + 4 <= hi && t != 0xFFFFu) {
-                uint4 v = vn;
-                if (i + 8 <= hi) vn = *reinterpret_cast<const uint4 *>(cand + i + 4);
-                walk_one(v.x, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
-                walk_one(v.y, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
-                walk_one(v.z, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
-                walk_one(v.w, t, qw, cw, cwn, last, evt, missb, os, om, qwords);
-                *reinterpret_cast<uint4 *>(cand + i) = v;
-                i += 4;
+    bool done = false;
+    int32_t rounds = n + (qwords >> 5) + 2;
+    // sweep position s (0 <= s < n) is candidate index (n0 + s) mod n
+    auto index_of = [&](int32_t s) { return n0 + s >= n ? n0 + s - n : n0 + s; };
+    uint32_t xnext = lane < n ? cand[index_of(lane)] : 0u;
+    for (int32_t s0 = 0; s0 < n && !done; s0 += 32) {
+        const uint32_t xv = xnext;
+        const uint32_t f = xv >> 16;
+        const int32_t cnt = min(32, n - s0);
+        const int32_t my = index_of(s0 + lane < n ? s0 + lane : 0);
+        if (s0 + 32 + lane < n) xnext = cand[index_of(s0 + 32 + lane)];  // next batch, loaded ahead
+        int cur = 0;
+        while (cur < cnt) {
+            if (--rounds < 0) return false;
+            const int32_t w0 = tq >> 5;
+            const uint32_t low = 0xFFFFFFFFu << (tq & 31);  // word w0: positions >= tq
+            uint32_t W = w0 + lane < qwords ? missb[w0 + lane] : 0u;
+            if (lane == 0) W &= low;
+            const int32_t wf = f == kNone16 ? 32 : static_cast<int32_t>(f >> 5) - w0;  // lookup's word
+            uint32_t ws = wf >= 0 && wf < 32 && w0 + wf < qwords ? missb[w0 + wf] : 0u;
+            if (wf == 0) ws &= low;
+            const uint32_t pop = static_cast<uint32_t>(__popc(W));
+            // the words' miss counts, bit-sliced over six ballots (counts are 0..32)
+            uint32_t bs[6];
+#pragma unroll
+            for (int b = 0; b < 6; ++b) bs[b] = __ballot_sync(kAll, (pop >> b) & 1u);
+            auto before = [&](uint32_t lanes) {  // misses in the words of `lanes`
+                int32_t c = 0;
+#pragma unroll
+                for (int b = 0; b < 6; ++b) c += __popc(bs[b] & lanes) << b;
+                return c;
+            };
+            const int32_t mtot = before(kAll);
+            if (mtot == 0) {  // no queued miss in these 32 words
+                if (w0 + 32 >= qwords) {
+                    done = true;
+                    break;
+                }
+                tq = (w0 + 32) << 5;
+                continue;
             }
+            const int32_t mw = min(32, mtot);
+            const bool live = lane >= cur && lane < cnt;
+            int32_t tj = 0;
+            if (live)
+                tj = wf >= 32 ? mw
+                              : (wf < 0 ? 0 : min(mw, before((1u << wf) - 1u) + __popc(ws & ((1u << (f & 31)) - 1u))));
+            // t_j = 0 always passes and t_j = mw always evicts once reached; only a lane whose
+            // lookup falls inside the window needs its k_j first, taken in lane order.
+            uint32_t evm = __ballot_sync(kAll, live && tj >= mw);
+            uint32_t am = __ballot_sync(kAll, live && tj > 0 && tj < mw);
+            while (am) {
+                const int a = __ffs(am) - 1;
+                am &= am - 1u;
+                const int32_t ta = __shfl_sync(kAll, tj, a);
+                if (__popc(evm & ((1u << a) - 1u)) < ta) evm |= 1u << a;
+            }
+            const int32_t myk = __popc(evm & ((1u << lane) - 1u));
+            const bool reached = live && myk < mw;
+            const bool ev = reached && ((evm >> lane) & 1u);
+            // arrival: the window's miss number myk. Its word is the last non-empty word whose
+            // first miss number is <= myk: marks (bit = first miss number of each non-empty
+            // word) count them, and the non-empty words' ballot gives its lane.
+            const int32_t e_me = before((1u << lane) - 1u);
+            const uint32_t nonempty = __ballot_sync(kAll, pop != 0u);
+            const uint32_t marks = __reduce_or_sync(kAll, pop != 0u && e_me < 32 ? 1u << e_me : 0u);
+            const int32_t r = min(myk, 31);
+            const int lo = select_bit(nonempty, __popc(marks & (0xFFFFFFFFu >> (31 - r))) - 1);
+            uint32_t x = w0 + lo < qwords ? missb[w0 + lo] : 0u;
+            if (lo == 0) x &= low;
+            const int pos = select_bit(x, r - before((1u << lo) - 1u));
+            const uint32_t arr = reached ? static_cast<uint32_t>(((w0 + lo) << 5) + pos) : 0xFFFFFFFFu;
+            const uint32_t cmin = __reduce_min_sync(kAll, ev && f != kNone16 ? f : 0xFFFFFFFFu);
+            const bool com = reached && arr < cmin;
+            const uint32_t cm = __ballot_sync(kAll, com);
+            const uint32_t slot = xv & 0xFFFFu;
+            if (com) {
+                cand[my] = (arr << 16) | slot;
+                if (ev) {
+                    os[arr] = static_cast<int32_t>(slot);
+                    om[arr] = 1;
+                    evt[slot] = static_cast<uint16_t>(arr);
+                    if (f != kNone16) atomicOr(&missb[f >> 5], 1u << (f & 31));  // created miss
+                }
+            }
+            // the last eviction committed (arrival times rise along the lanes): +1 so 0 = none
+            const uint32_t le = __reduce_max_sync(kAll, com && ev ? ((arr << 16) | slot) + 1u : 0u);
+            if (le) {
+                last = static_cast<int32_t>((le - 1u) & 0xFFFFu);
+                tq = static_cast<int32_t>((le - 1u) >> 16) + 1;
+            }
+            if (cm == 0u) return false;  // cannot happen: the first lane is always committed
+            cur = 32 - __clz(cm);
+            __syncwarp();  // created misses visible before the next round reads the queue
         }
-        // tail
-        for (; i < hi && t != 0xFFFFu; ++i) walk_one(cand[i], t, qw, cw, cwn, last, evt, missb, os, om, qwords);
     }
-    if (t != 0xFFFFu) return false;  // every candidate passed once: the sweep would wrap
+    if (!done) {  // every candidate was visited: misses left over mean the sweep would wrap
+        bool rem = false;
+        for (int32_t w = (tq >> 5) + lane; w < qwords; w += 32) {
+            uint32_t W = missb[w];
+            if (w == (tq >> 5)) W &= 0xFFFFFFFFu << (tq & 31);
+            rem |= W != 0u;
+        }
+        if (__any_sync(kAll, rem)) return false;
+    }
     *last_out = last;
     return true;
 }
@@ -680,12 +753,12 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     }
     __syncthreads();
 
-    // ---- phase 2: the hand sweep (candidate list, one-thread walk, final bits) ----
+    // ---- phase 2: the hand sweep (candidate list, warp walk, final bits) ----
     uint32_t *s_cand = reinterpret_cast<uint32_t *>(smem + L.dkey);  // dedup table no longer needed
     uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
     if (!s_flag) build_candidates(s_vini, s_tf, s_cand, s_wofs, dbs, &s_ncand, s_warp);
     __syncthreads();
-    if (!s_flag && tid == 0) {
+    if (!s_flag && tid < 32) {
         const int32_t n = s_ncand;
         const int32_t h0 = s_hand;
         // first candidate at or after the hand, in slot order
@@ -693,9 +766,12 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
                      __popc(~s_vini[h0 >> 5] & ((1u << (h0 & 31)) - 1u));
         if (n0 >= n) n0 = 0;
         int32_t last = -1;
-        if (!walk_candidates(s_cand, n, n0, s_evt, s_missb, s_os, s_om, K, &last)) s_flag = 1;
-        s_last = last;
-        s_any_miss = last >= 0;
+        const bool ok = walk_candidates(s_cand, n, n0, s_evt, s_missb, s_os, s_om, K, &last);
+        if (tid == 0) {
+            if (!ok) s_flag = 1;
+            s_last = last;
+            s_any_miss = last >= 0;
+        }
     }
     __syncthreads();
     if (!s_flag && s_last >= 0) {
