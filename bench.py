@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers per decode step (61 = config 2)")
+    ap.add_argument("--path", choices=["auto", "coop", "fused", "split"], default="auto",
+                    help="layer-step path of sieve_and_read (auto: cooperative when it fits)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -238,22 +240,19 @@ def run_b200(args):
     co.admit_all(pre, base)
 
     stream = torch.cuda.current_stream(dev).cuda_stream
-
-    def layer_step(s, l, ev=None):
-        if ev is not None:
-            ev[0].record()
-        co.sieve_update(l, topk[s, l], stream=stream)
-        if ev is not None:
-            ev[1].record()
-        pool.batch_read(l, topk[s, l], co._req_pool_indices, co.req_host_base, co.top_k_device_slots, co.is_miss,
-                        co.num_real, hot[l], R, K, stream, 1, fused=True, hot_req_stride_rows=dbs)
-        if ev is not None:
-            ev[2].record()
+    # The public one-call layer-step (DevicePool.sieve_and_read, path "auto"): one cooperative
+    # launch whose non-SIEVE CTAs copy each request's miss rows as soon as its hand sweep is
+    # done (or, where that does not fit, the SIEVE kernel and the gather as its programmatic
+    # dependent).
+    def layer_step(s, l):
+        pool.sieve_and_read(co, l, topk[s, l], hot[l], stream, 1, hot_req_stride_rows=dbs, path=args.path)
 
     for s in range(W):
         for l in range(L):
             layer_step(s, l)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(S * L)]
+    path = mod.last_step_path()
+    fused = path in ("coop", "fused")  # one kernel per layer-step
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(S * L)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(torch, local)
     clocks.start()
@@ -263,7 +262,10 @@ def run_b200(args):
     t0.record()
     for s in range(W, T):
         for l in range(L):
-            layer_step(s, l, evs[(s - W) * L + l])
+            e = evs[(s - W) * L + l]
+            e[0].record()
+            layer_step(s, l)
+            e[1].record()
     t1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -272,15 +274,43 @@ def run_b200(args):
     last = int(co.is_miss.sum().item())
     assert last == int(misses_h[T - 1, L - 1]), "replay diverged from the input pass"
     elapsed = t0.elapsed_time(t1) * 1e-3
-    sieve_us = [e[0].elapsed_time(e[1]) * 1e3 for e in evs]
-    gather_us = [e[1].elapsed_time(e[2]) * 1e3 for e in evs]
-    step_us = [e[0].elapsed_time(e[2]) * 1e3 for e in evs]
+    step_us = [e[0].elapsed_time(e[1]) * 1e3 for e in evs]
     miss_rows = int(misses_h[W:].sum())
 
-    e2e = None if args.no_e2e else run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev)
+    # Kernel durations for the roofline: the same steps replayed from the admitted state with
+    # an event around each kernel (an event between the two kernels also stops the gather from
+    # launching early, so this pass is not the timed one).
+    co.admit_all(pre, base)
+    kev = []
+    for s in range(T):
+        for l in range(L):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            if fused:
+                layer_step(s, l)
+                e[1].record()
+            else:
+                co.sieve_update(l, topk[s, l], stream=stream)
+                e[1].record()
+                pool.batch_read(l, topk[s, l], co._req_pool_indices, co.req_host_base, co.top_k_device_slots,
+                                co.is_miss, co.num_real, hot[l], R, K, stream, 1, fused=True, hot_req_stride_rows=dbs)
+            e[2].record()
+            if s >= W:
+                kev.append(e)
+    torch.cuda.synchronize()
+    assert int(co.is_miss.sum().item()) == last, "kernel pass diverged"
+    if fused:
+        kernels = {"sieve_fast_kernel<{}>".format(2 if path == "coop" else 1):
+                   [e[0].elapsed_time(e[1]) * 1e3 for e in kev]}
+    else:
+        kernels = {"sieve_fast_kernel": [e[0].elapsed_time(e[1]) * 1e3 for e in kev],
+                   "gather_kernel": [e[1].elapsed_time(e[2]) * 1e3 for e in kev]}
 
-    res = dict(elapsed=elapsed, miss_rows=miss_rows, sieve_us=sieve_us, gather_us=gather_us, step_us=step_us,
-               e2e=e2e, clocks=clk, nodes=len(nodes))
+    e2e = None if args.no_e2e else run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev,
+                                                   args.path)
+
+    res = dict(elapsed=elapsed, miss_rows=miss_rows, kernels=kernels, step_us=step_us, e2e=e2e, clocks=clk,
+               nodes=len(nodes), fused=fused, path=path)
     if world > 1:
         gathered = [None] * world
         dist.all_gather_object(gathered, res)
@@ -297,11 +327,12 @@ def run_b200(args):
         report_b200(args, world, gathered, co)
 
 
-def run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev):
+def run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs, dev, path):
     """The same decode steps through the public API with host inputs: each step copies its
-    topK tensors from pinned host memory, runs every layer's sieve_update + batch_read and waits
-    on the status slots (the reference driver's loop, xds_decode.py:226-236), then reads the
-    per-layer miss counts back to the host. Host wall clock around the K timed steps."""
+    topK tensors from pinned host memory, runs every layer's sieve_and_read (the reference
+    driver's sieve_update + batch_read pair, xds_decode.py:226-236, in one call) and waits on
+    the status slots, then reads the per-layer miss counts back to the host. Host wall clock
+    around the K timed steps."""
     T = W + S
     topk_host = topk.cpu().pin_memory()
     buf = torch.empty((L, R, K), dtype=torch.int32, device=dev)
@@ -313,10 +344,8 @@ def run_e2e(torch, co, pool, hot, topk, misses_h, pre, base, L, W, S, R, K, dbs,
     def step(s):
         buf.copy_(topk_host[s], non_blocking=True)
         for l in range(L):
-            co.sieve_update(l, buf[l], stream=stream.cuda_stream)
-            st = pool.batch_read(l, buf[l], co._req_pool_indices, co.req_host_base, co.top_k_device_slots,
-                                 co.is_miss, co.num_real, hot[l], R, K, stream.cuda_stream, 1, fused=True,
-                                 hot_req_stride_rows=dbs)
+            st = pool.sieve_and_read(co, l, buf[l], hot[l], stream.cuda_stream, 1, hot_req_stride_rows=dbs,
+                                     path=path)
             pool.wait(st)
             counts[l] = co.is_miss.sum()
         counts_h.copy_(counts, non_blocking=True)
@@ -352,32 +381,43 @@ def report_b200(args, world, gathered, co):
     miss_rows = sum(g["miss_rows"] for g in gathered)
     value = miss_rows * ROW_BYTES / elapsed / 1e9
     g0 = gathered[0]
-    n = len(g0["sieve_us"])
-    sieve_avg = sum(g0["sieve_us"]) / n
-    gather_avg = sum(g0["gather_us"]) / n
+    kern = {k: sum(v) / len(v) for k, v in g0["kernels"].items()}
+    n = len(g0["step_us"])
     rows_per_launch = g0["miss_rows"] / n
     remote = world > 1
     tr = traffic_per_unit()
-    # Gather: payload read + write (local pool) or NVLink ingress (peer pool), plus 9 B of
-    # metadata per position and 16 B per request.
-    meta = R * K * 9 + R * 16
-    if remote:
-        g_bytes, g_peak, g_bound, g_kind = rows_per_launch * ROW_BYTES, 770.0, "nvlink", "peer-copy 770 GB/s/dir"
-    else:
-        g_bytes, g_peak, g_bound, g_kind = rows_per_launch * 2 * ROW_BYTES + meta, hbm_peak, "hbm", peak_kind
     sb = state_bytes(co.padded_buffer_size, co.visited_stride_b, co.ht_size)
-    s_bytes = R * (2 * sb + 9 * K)
-    roof_gather = {"kernel": "gather_kernel", "bound": g_bound, "achieved": g_bytes / (gather_avg * 1e-6) / 1e9,
-                   "peak": g_peak, "unit": "GB/s", "peak_source": g_kind,
-                   "traffic": tr["gather_per_row"] * rows_per_launch if "gather_per_row" in tr else None,
-                   "algorithmic_bytes": g_bytes, "avg_us": gather_avg}
-    roof_gather["frac"] = roof_gather["achieved"] / g_peak
-    roof_sieve = {"kernel": "sieve_fast_kernel", "bound": "hbm", "achieved": s_bytes / (sieve_avg * 1e-6) / 1e9,
-                  "peak": hbm_peak, "unit": "GB/s", "peak_source": peak_kind,
-                  "traffic": tr["sieve_per_request"] * R if "sieve_per_request" in tr else None,
-                  "algorithmic_bytes": s_bytes, "avg_us": sieve_avg}
-    roof_sieve["frac"] = roof_sieve["achieved"] / hbm_peak
-    dominant, other = (roof_sieve, roof_gather) if sieve_avg >= gather_avg else (roof_gather, roof_sieve)
+    s_bytes = R * (2 * sb + 9 * K)  # SIEVE state read + written, topK read, slots + flags written
+    # Gather: payload read + write (local pool), plus 9 B of metadata per position and 16 B per
+    # request; from peer pools the bound is the NVLink ingress of the payload.
+    meta = R * K * 9 + R * 16
+    hbm_gather = rows_per_launch * 2 * ROW_BYTES + meta
+
+    def roof(kernel, bound, nbytes, avg_us, peak, peak_source, traffic):
+        return {"kernel": kernel, "bound": bound, "achieved": nbytes / (avg_us * 1e-6) / 1e9, "peak": peak,
+                "unit": "GB/s", "frac": nbytes / (avg_us * 1e-6) / 1e9 / peak, "peak_source": peak_source,
+                "traffic": traffic, "algorithmic_bytes": nbytes, "avg_us": avg_us}
+
+    if g0["fused"]:
+        (name, t), = kern.items()
+        hbm_bytes = s_bytes + hbm_gather
+        if remote:  # rows cross NVLink; this GPU's HBM holds the state and the hot rows
+            dominant = roof(name, "nvlink", rows_per_launch * ROW_BYTES, t, 770.0,
+                            "peer copy 770 GB/s per direction (measured on this pool)", None)
+            other = roof(name + ", HBM side", "hbm", s_bytes + rows_per_launch * ROW_BYTES + meta, t, hbm_peak,
+                         peak_kind, None)
+        else:
+            traffic = None
+            if "gather_per_row" in tr and "sieve_per_request" in tr:
+                traffic = tr["gather_per_row"] * rows_per_launch + tr["sieve_per_request"] * R
+            dominant = roof(name, "hbm", hbm_bytes, t, hbm_peak, peak_kind, traffic)
+            other = None
+    else:
+        rs = roof("sieve_fast_kernel", "hbm", s_bytes, kern["sieve_fast_kernel"], hbm_peak, peak_kind,
+                  tr["sieve_per_request"] * R if "sieve_per_request" in tr else None)
+        rg = roof("gather_kernel", "hbm", hbm_gather, kern["gather_kernel"], hbm_peak, peak_kind,
+                  tr["gather_per_row"] * rows_per_launch if "gather_per_row" in tr else None)
+        dominant, other = (rs, rg) if rs["avg_us"] >= rg["avg_us"] else (rg, rs)
     steps_all = [x for g in gathered for x in g["step_us"]]
     out = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -390,13 +430,16 @@ def report_b200(args, world, gathered, co):
                        world - 1),
                    "l2": "inputs larger than L2 (SIEVE state {:.0f} MB, pool {:.1f} GB per GPU)".format(
                        L * R * sb / 1e6, L * R * CFG["ctx"] * ROW_BYTES / 1e9),
-                   "step": "one decode step = {} layers x (sieve_update + gather)".format(L)},
+                   "step": "one decode step = {} layers x sieve_and_read, path {} ({})".format(
+                       L, g0["path"], {"coop": "one cooperative kernel: SIEVE CTAs + row-copy CTAs",
+                                       "fused": "one kernel: SIEVE + bulk-copy warp",
+                                       "split": "SIEVE kernel + gather as programmatic dependent"}[g0["path"]])},
         "p50_us_per_layer_step": pct(steps_all, 50), "p99_us_per_layer_step": pct(steps_all, 99),
-        "sieve_p50_us": pct(g0["sieve_us"], 50), "gather_p50_us": pct(g0["gather_us"], 50),
-        "gather_only_gbs": g0["miss_rows"] * ROW_BYTES / (sum(g0["gather_us"]) * 1e-6) / 1e9,
+        "kernel_avg_us": kern,
+        "kernel_timing": "separate replay of the same steps with CUDA events around each kernel",
         "miss_rows_per_layer_step": rows_per_launch,
         "roofline": dominant, "roofline_other": other,
-        "gpu_launches": 2 * L * args.steps,
+        "gpu_launches": (1 if g0["fused"] else 2) * L * args.steps,
         "clocks": g0["clocks"],
     }
     if g0["e2e"] is not None:

@@ -42,6 +42,7 @@ extern "C" {
 /* Device-side errCode bands (kvops/kernel/kvc_common.h:24). */
 #define KVOPS_ERR_SEG_NULL 0x101u  /* segment base is 0: nothing touched (0x1xx, init band) */
 #define KVOPS_ERR_ROW_BASE 0x200u  /* 0x200 + (index & 0xFF) + (1 << 16): row out of the segment */
+#define KVOPS_ERR_COPY_TIMEOUT 0x102u  /* kvops_sieve_import: a row copy did not complete (not expected) */
 
 /* Largest node count of one layout (common/kv_layout.h:45, KvLayoutValidate). */
 #define KVOPS_MAX_NODES 64
@@ -90,8 +91,21 @@ typedef struct KvopsRowOpts {
      * 1: segRow = ((row/S)/N)*S + row%S (injective; per_layer_seg_rows must then be
      *    ceil(ceil(layer_rows/S)/N)*S). */
     uint32_t injective;
-    uint32_t reserved;
+    /* kvops_sieve_import only (ignored elsewhere): how the layer-step runs. Every path gives the
+     * same results; a path that does not fit the shapes falls back to SPLIT.
+     * COOP: one cooperative launch; the SIEVE CTAs publish their outputs after the hand sweep and
+     *   the other CTAs resident on the GPU copy the miss rows meanwhile (16-byte aligned rows).
+     * FUSED: one launch; a copy warp in each SIEVE CTA moves its rows by bulk copies (device
+     *   memory segments only).
+     * SPLIT: the SIEVE kernel, then the gather launched as its programmatic dependent.
+     * AUTO: COOP when it fits, else SPLIT. */
+    uint32_t step_path;
 } KvopsRowOpts;
+
+#define KVOPS_STEP_AUTO 0u
+#define KVOPS_STEP_FUSED 1u
+#define KVOPS_STEP_SPLIT 2u
+#define KVOPS_STEP_COOP 3u
 
 /* kvops_import_seg with options (opts may be NULL). */
 int kvops_import_seg_ex(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
@@ -150,6 +164,25 @@ int kvops_sieve_ht_init(uint64_t device_buffer_tokens, uint64_t device_buffer_ht
                         uint32_t req_start, uint32_t num_reqs, uint32_t layer_num, uint32_t pool_size,
                         uint32_t device_buffer_size, uint32_t padded_buffer_size, uint32_t ht_size,
                         uint64_t stream, uint32_t block_dim);
+
+/* One decode layer-step in one call: kvops_sieve_update followed by kvops_import_multi over
+ * the same tensors, with identical results (slots, miss flags, SIEVE state, hot rows, status
+ * words, errCodes). No counterpart in the reference, whose driver issues the two calls
+ * (xds/xds_decode.py:225-233). opts->step_path chooses how (KVOPS_STEP_*, default AUTO).
+ * block_dim: status words per node (1..8), as in kvops_import_multi. A row copy that never
+ * completes, or a request whose outputs never become ready, sets errCode KVOPS_ERR_COPY_TIMEOUT. */
+int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_lens, uint64_t prefill_lens,
+                       uint64_t device_buffer_tokens, uint64_t device_buffer_visited, uint64_t device_buffer_ht,
+                       uint64_t sieve_hand, uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real,
+                       uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
+                       uint32_t visited_stride_b, uint32_t max_num_reqs, uint32_t pool_size, uint32_t node_num,
+                       const uint64_t *seg_bases, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
+                       uint32_t row_bytes, uint64_t req_host_base, uint64_t hot_row_base, uint32_t stripe_rows,
+                       uint64_t status, uint64_t stream, uint32_t block_dim, const KvopsRowOpts *opts);
+
+/* KVOPS_STEP_COOP, _FUSED or _SPLIT: the path the calling thread's last successful
+ * kvops_sieve_import ran (KVOPS_STEP_AUTO before any). No counterpart in the reference. */
+uint32_t kvops_last_step_path(void);
 
 /* No counterpart in the reference. kvops_import_multi for callers that cannot allocate
  * device memory (an engine whose HBM is owned by its own allocator or fixed budget, or a

@@ -21,7 +21,8 @@ C_ABI_SYMBOLS = (
     "kvops_import_seg", "kvops_import_seg_ex", "kvops_import_multi", "kvops_export_seg_alllayer",
     "kvops_export_seg_alllayer_ex", "kvops_sieve_update", "kvops_sieve_ht_init", "kvops_segment_alloc",
     "kvops_segment_free", "kvops_enable_peer_access", "kvops_ipc_get_handle", "kvops_ipc_open_handle",
-    "kvops_ipc_close_handle", "kvops_import_multi_noalloc",
+    "kvops_ipc_close_handle", "kvops_import_multi_noalloc", "kvops_sieve_import",
+    "kvops_last_step_path",
 )
 
 _lib = None

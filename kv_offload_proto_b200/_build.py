@@ -37,12 +37,12 @@ def _run(cmd):
 
 
 def build_lib(force=False, verbose_ptxas=False):
-    deps = [os.path.join(CSRC, f) for f in CU_SOURCES + ["kvops_internal.cuh"]]
+    deps = [os.path.join(CSRC, f) for f in CU_SOURCES + ["kvops_internal.cuh", "rows_common.cuh"]]
     deps.append(os.path.join(ROOT, "include", "kvops_b200.h"))
     if not force and not _newer(LIB, deps):
         return LIB
     cmd = [NVCC, "-O3", "-std=c++17", "-lineinfo", *ARCH, "-Xcompiler", "-fPIC", "-shared",
-           "-I", os.path.join(ROOT, "include"), "-o", LIB]
+           "-Xlinker", "--no-undefined", "-I", os.path.join(ROOT, "include"), "-o", LIB]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     cmd += [os.path.join(CSRC, f) for f in CU_SOURCES]

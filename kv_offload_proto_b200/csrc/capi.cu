@@ -43,9 +43,16 @@ struct DeviceState {
     uint32_t ring_size = 0;
     std::atomic<uint32_t> next{0};
     int sm_count = 0;
+    uint32_t *ready = nullptr;  // cooperative layer-steps: kReadyBlocks blocks of kReadyWords words
+    std::atomic<uint32_t> ready_next{0};
 };
 
+// Ready words of cooperative layer-steps: launch n uses block n % kReadyBlocks, so a block is
+// reused only after kReadyBlocks later launches; the kernel keeps each block's epoch itself.
+constexpr uint32_t kReadyBlocks = 4096, kReadyWords = 256;
+
 std::mutex g_mu;
+thread_local uint32_t t_last_step_path = KVOPS_STEP_AUTO;  // path the last kvops_sieve_import ran
 bool g_inited = false;
 int g_home_device = 0;
 std::vector<void *> g_status_allocs;
@@ -133,12 +140,12 @@ int make_status_target(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint
         if (!g_inited) return fail(KVOPS_E_NOT_INITED, "kvops not inited"); \
     } while (0)
 
-int import_common(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo, uint32_t node_hi,
+int build_gather(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo, uint32_t node_hi,
                   uint32_t my_node, uint32_t layer_offset_rows, uint32_t plsr, uint32_t row_bytes,
                   uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
                   uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base,
                   uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
-                  uint32_t block_dim, const KvopsRowOpts *opts)
+                  uint32_t block_dim, const KvopsRowOpts *opts, kvb::GatherParams *out, DeviceState **ds_out)
 {
     KV_REQUIRE_INIT();
     if (block_dim > 8) return fail(KVOPS_E_INVALID, "import blockDim must be <= 8 (status slot layout)");
@@ -180,6 +187,25 @@ int import_common(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo
     rc = make_status_target(status, node_lo, node_hi, block_dim, ds, &p.st);
     if (rc != KVOPS_OK) return rc;
     if (max_num_reqs == 0 || top_k == 0) p.num_real = nullptr;  // nothing to scan: still completes the status
+    (void)stream;
+    *out = p;
+    *ds_out = ds;
+    return KVOPS_OK;
+}
+
+int import_common(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo, uint32_t node_hi,
+                  uint32_t my_node, uint32_t layer_offset_rows, uint32_t plsr, uint32_t row_bytes,
+                  uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
+                  uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base,
+                  uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
+                  uint32_t block_dim, const KvopsRowOpts *opts)
+{
+    kvb::GatherParams p{};
+    DeviceState *ds = nullptr;
+    int rc = build_gather(node_num, seg_bases, node_lo, node_hi, my_node, layer_offset_rows, plsr, row_bytes,
+                          topk_indices, req_pool_indices, req_host_base, topk_device_slots, is_miss, num_real,
+                          hot_row_base, top_k, max_num_reqs, stripe_rows, status, stream, block_dim, opts, &p, &ds);
+    if (rc != KVOPS_OK) return rc;
     cudaError_t e = kvb::launch_gather(p, reinterpret_cast<cudaStream_t>(stream), ds->sm_count);
     if (e != cudaSuccess) return cuda_fail(e, "launch kvc_gather_rows");
     return KVOPS_OK;
@@ -244,6 +270,121 @@ int export_common(uint64_t seg_base, uint32_t plsr, uint32_t row_bytes, uint32_t
     return KVOPS_OK;
 }
 
+int build_sieve(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_lens, uint64_t prefill_lens,
+                       uint64_t device_buffer_tokens, uint64_t device_buffer_visited, uint64_t device_buffer_ht,
+                       uint64_t sieve_hand, uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real,
+                       uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
+                       uint32_t visited_stride_b, uint32_t max_num_reqs, uint32_t pool_size, uint64_t stream,
+                       uint32_t block_dim, kvb::SieveParams *out, DeviceState **ds_out)
+{
+    KV_REQUIRE_INIT();
+    // Validation of kvops_ext.cpp:288-296, in the same order and with the same messages.
+    if (padded_buffer_size % 16 != 0)
+        return fail(KVOPS_E_INVALID, "sieve_update: padded_buffer_size must be a multiple of 16 (64-byte rows)");
+    if (padded_buffer_size > 65534)
+        return fail(KVOPS_E_INVALID, "sieve_update: padded_buffer_size must be <= 65534 (uint16 hash slots)");
+    if (visited_stride_b % 64 != 0 || visited_stride_b < (padded_buffer_size + 7) / 8)
+        return fail(KVOPS_E_INVALID, "sieve_update: visited bitmap stride must be 64B aligned and cover padded");
+    // Domain checks the reference leaves to its callers (a zero block_dim divides by zero
+    // there, kvops_ext.cpp:308; dbs outside [1, padded] indexes past the token row).
+    if (block_dim == 0) return fail(KVOPS_E_INVALID, "sieve_update: block_dim must be >= 1");
+    if (device_buffer_size == 0 || device_buffer_size > padded_buffer_size)
+        return fail(KVOPS_E_INVALID, "sieve_update: device_buffer_size must be in [1, padded_buffer_size]");
+    if (top_k > (1u << 24) || max_num_reqs > (1u << 24))
+        return fail(KVOPS_E_INVALID, "sieve_update: top_k / max_num_reqs out of range");
+    int64_t ht_size = 1024;  // kvops_ext.cpp:297-300
+    while (ht_size < 2 * (static_cast<int64_t>(padded_buffer_size) + top_k)) ht_size <<= 1;
+    *ds_out = nullptr;
+    if (max_num_reqs == 0 || top_k == 0) return KVOPS_OK;  // nothing to do (*ds_out stays null)
+    if (topk_indices == 0 || req_pool_indices == 0 || seq_lens == 0 || prefill_lens == 0 ||
+        device_buffer_tokens == 0 || device_buffer_visited == 0 || device_buffer_ht == 0 || sieve_hand == 0 ||
+        topk_device_slots == 0 || is_miss == 0 || num_real == 0)
+        return fail(KVOPS_E_INVALID, "sieve_update: a tensor address is 0");
+    DeviceState *ds = nullptr;
+    int rc = current_device_state(&ds);
+    if (rc != KVOPS_OK) return rc;
+    kvb::SieveParams p{};
+    p.topk = reinterpret_cast<const int32_t *>(topk_indices);
+    p.req_pool = reinterpret_cast<const int64_t *>(req_pool_indices);
+    p.seq_lens = reinterpret_cast<const int32_t *>(seq_lens);
+    p.prefill = reinterpret_cast<const int32_t *>(prefill_lens);
+    p.tokens = reinterpret_cast<int32_t *>(device_buffer_tokens);
+    p.visited = reinterpret_cast<uint8_t *>(device_buffer_visited);
+    p.ht = reinterpret_cast<uint16_t *>(device_buffer_ht);
+    p.hand = reinterpret_cast<int32_t *>(sieve_hand);
+    p.out_slots = reinterpret_cast<int32_t *>(topk_device_slots);
+    p.is_miss = reinterpret_cast<int8_t *>(is_miss);
+    p.num_real = reinterpret_cast<const int32_t *>(num_real);
+    p.top_k = static_cast<int32_t>(top_k);
+    p.dbs = static_cast<int32_t>(device_buffer_size);
+    p.padded = static_cast<int32_t>(padded_buffer_size);
+    p.vis_stride = static_cast<int32_t>(visited_stride_b);
+    p.max_num_reqs = static_cast<int32_t>(max_num_reqs);
+    p.pool_size = static_cast<int32_t>(pool_size);
+    p.ht_size = static_cast<int32_t>(ht_size);
+    (void)stream;
+    *out = p;
+    *ds_out = ds;
+    return KVOPS_OK;
+}
+
+// Whether every row of a gather can move as 16-byte chunks (the copy helpers' width).
+bool vec16_ok(const kvb::GatherParams &g)
+{
+    uint64_t a = g.row_bytes | reinterpret_cast<uintptr_t>(g.hot) | g.hot_req_stride_bytes;
+    for (uint32_t n = 0; n < g.nodes; ++n) a |= reinterpret_cast<uintptr_t>(g.seg[n]);
+    return (a & 15) == 0;
+}
+
+// The ready words for the next cooperative layer-step on this device.
+int next_ready_block(DeviceState *ds, uint32_t **words)
+{
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ds->ready == nullptr) {
+            const size_t bytes = sizeof(uint32_t) * kReadyBlocks * kReadyWords;
+            cudaError_t e = cudaMalloc(&ds->ready, bytes);
+            if (e != cudaSuccess) {
+                ds->ready = nullptr;
+                return cuda_fail(e, "cudaMalloc(ready words)");
+            }
+            e = cudaMemset(ds->ready, 0, bytes);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(ready words)");
+        }
+    }
+    const uint32_t n = ds->ready_next.fetch_add(1, std::memory_order_relaxed);
+    *words = ds->ready + static_cast<size_t>(n % kReadyBlocks) * kReadyWords;
+    return KVOPS_OK;
+}
+
+// Whether every row copy of the fused step may be a bulk copy: 16-byte multiples and
+// alignment on both sides, and every segment in device memory (own or peer HBM). *remote is
+// set when a segment is on another GPU.
+bool bulk_copy_ok(const kvb::GatherParams &g, bool *remote)
+{
+    *remote = false;
+    if (g.row_bytes % 16 != 0 || reinterpret_cast<uintptr_t>(g.hot) % 16 != 0 || g.hot_req_stride_bytes % 16 != 0)
+        return false;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    for (uint32_t n = 0; n < g.nodes; ++n) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(g.seg[n]);
+        if (a == 0) continue;  // reported as KVOPS_ERR_SEG_NULL, never read
+        if (a % 16 != 0) return false;
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, g.seg[n]) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (at.type != cudaMemoryTypeDevice) return false;
+        if (at.device != dev) *remote = true;
+    }
+    return true;
+}
+
 }  // namespace
 
 namespace kvb {
@@ -287,6 +428,7 @@ int kvops_close(void)
     for (auto &kv : g_devices) {
         cudaSetDevice(kv.first);
         cudaFree(kv.second->ring);
+        if (kv.second->ready) cudaFree(kv.second->ready);
         delete kv.second;
     }
     g_devices.clear();
@@ -433,54 +575,81 @@ int kvops_sieve_update(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
                        uint32_t visited_stride_b, uint32_t max_num_reqs, uint32_t pool_size, uint64_t stream,
                        uint32_t block_dim)
 {
-    KV_REQUIRE_INIT();
-    // Validation of kvops_ext.cpp:288-296, in the same order and with the same messages.
-    if (padded_buffer_size % 16 != 0)
-        return fail(KVOPS_E_INVALID, "sieve_update: padded_buffer_size must be a multiple of 16 (64-byte rows)");
-    if (padded_buffer_size > 65534)
-        return fail(KVOPS_E_INVALID, "sieve_update: padded_buffer_size must be <= 65534 (uint16 hash slots)");
-    if (visited_stride_b % 64 != 0 || visited_stride_b < (padded_buffer_size + 7) / 8)
-        return fail(KVOPS_E_INVALID, "sieve_update: visited bitmap stride must be 64B aligned and cover padded");
-    // Domain checks the reference leaves to its callers (a zero block_dim divides by zero
-    // there, kvops_ext.cpp:308; dbs outside [1, padded] indexes past the token row).
-    if (block_dim == 0) return fail(KVOPS_E_INVALID, "sieve_update: block_dim must be >= 1");
-    if (device_buffer_size == 0 || device_buffer_size > padded_buffer_size)
-        return fail(KVOPS_E_INVALID, "sieve_update: device_buffer_size must be in [1, padded_buffer_size]");
-    if (top_k > (1u << 24) || max_num_reqs > (1u << 24))
-        return fail(KVOPS_E_INVALID, "sieve_update: top_k / max_num_reqs out of range");
-    int64_t ht_size = 1024;  // kvops_ext.cpp:297-300
-    while (ht_size < 2 * (static_cast<int64_t>(padded_buffer_size) + top_k)) ht_size <<= 1;
-    if (max_num_reqs == 0 || top_k == 0) return KVOPS_OK;
-    if (topk_indices == 0 || req_pool_indices == 0 || seq_lens == 0 || prefill_lens == 0 ||
-        device_buffer_tokens == 0 || device_buffer_visited == 0 || device_buffer_ht == 0 || sieve_hand == 0 ||
-        topk_device_slots == 0 || is_miss == 0 || num_real == 0)
-        return fail(KVOPS_E_INVALID, "sieve_update: a tensor address is 0");
-    DeviceState *ds = nullptr;
-    int rc = current_device_state(&ds);
-    if (rc != KVOPS_OK) return rc;
     kvb::SieveParams p{};
-    p.topk = reinterpret_cast<const int32_t *>(topk_indices);
-    p.req_pool = reinterpret_cast<const int64_t *>(req_pool_indices);
-    p.seq_lens = reinterpret_cast<const int32_t *>(seq_lens);
-    p.prefill = reinterpret_cast<const int32_t *>(prefill_lens);
-    p.tokens = reinterpret_cast<int32_t *>(device_buffer_tokens);
-    p.visited = reinterpret_cast<uint8_t *>(device_buffer_visited);
-    p.ht = reinterpret_cast<uint16_t *>(device_buffer_ht);
-    p.hand = reinterpret_cast<int32_t *>(sieve_hand);
-    p.out_slots = reinterpret_cast<int32_t *>(topk_device_slots);
-    p.is_miss = reinterpret_cast<int8_t *>(is_miss);
-    p.num_real = reinterpret_cast<const int32_t *>(num_real);
-    p.top_k = static_cast<int32_t>(top_k);
-    p.dbs = static_cast<int32_t>(device_buffer_size);
-    p.padded = static_cast<int32_t>(padded_buffer_size);
-    p.vis_stride = static_cast<int32_t>(visited_stride_b);
-    p.max_num_reqs = static_cast<int32_t>(max_num_reqs);
-    p.pool_size = static_cast<int32_t>(pool_size);
-    p.ht_size = static_cast<int32_t>(ht_size);
+    DeviceState *ds = nullptr;
+    int rc = build_sieve(topk_indices, req_pool_indices, seq_lens, prefill_lens, device_buffer_tokens,
+                         device_buffer_visited, device_buffer_ht, sieve_hand, topk_device_slots, is_miss, num_real,
+                         top_k, device_buffer_size, padded_buffer_size, visited_stride_b, max_num_reqs, pool_size,
+                         stream, block_dim, &p, &ds);
+    if (rc != KVOPS_OK || ds == nullptr) return rc;
     cudaError_t e = kvb::launch_sieve_update(p, reinterpret_cast<cudaStream_t>(stream), ds->sm_count);
     if (e != cudaSuccess) return cuda_fail(e, "launch hisp_sieve_update");
     return KVOPS_OK;
 }
+
+int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_lens, uint64_t prefill_lens,
+                       uint64_t device_buffer_tokens, uint64_t device_buffer_visited, uint64_t device_buffer_ht,
+                       uint64_t sieve_hand, uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real,
+                       uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
+                       uint32_t visited_stride_b, uint32_t max_num_reqs, uint32_t pool_size, uint32_t node_num,
+                       const uint64_t *seg_bases, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
+                       uint32_t row_bytes, uint64_t req_host_base, uint64_t hot_row_base, uint32_t stripe_rows,
+                       uint64_t status, uint64_t stream, uint32_t block_dim, const KvopsRowOpts *opts)
+{
+    KV_REQUIRE_INIT();
+    if (node_num == 0 || node_num > KVOPS_MAX_NODES)
+        return fail(KVOPS_E_INVALID, "sieve_import node_num must be in [1, 64]");
+    if (seg_bases == nullptr) return fail(KVOPS_E_INVALID, "sieve_import: seg_bases is NULL");
+    kvb::SieveParams sp{};
+    DeviceState *sds = nullptr;  // null: the SIEVE step has nothing to do
+    int rc = build_sieve(topk_indices, req_pool_indices, seq_lens, prefill_lens, device_buffer_tokens,
+                         device_buffer_visited, device_buffer_ht, sieve_hand, topk_device_slots, is_miss, num_real,
+                         top_k, device_buffer_size, padded_buffer_size, visited_stride_b, max_num_reqs, pool_size,
+                         stream, 1u, &sp, &sds);
+    if (rc != KVOPS_OK) return rc;
+    kvb::GatherParams gp{};
+    DeviceState *ds = nullptr;
+    rc = build_gather(node_num, seg_bases, 0, node_num, kvb::kAllNodes, layer_offset_rows, per_layer_seg_rows,
+                      row_bytes, topk_indices, req_pool_indices, req_host_base, topk_device_slots, is_miss, num_real,
+                      hot_row_base, top_k, max_num_reqs, stripe_rows, status, stream, block_dim, opts, &gp, &ds);
+    if (rc != KVOPS_OK) return rc;
+    const uint32_t path = opts ? opts->step_path : KVOPS_STEP_AUTO;
+    if (path > KVOPS_STEP_COOP) return fail(KVOPS_E_INVALID, "sieve_import: step_path must be 0, 1, 2 or 3");
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (sds != nullptr && (path == KVOPS_STEP_AUTO || path == KVOPS_STEP_COOP) && vec16_ok(gp)) {
+        uint32_t *words = nullptr;
+        rc = next_ready_block(sds, &words);
+        if (rc != KVOPS_OK) return rc;
+        bool launched = false;
+        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, st, &launched);
+        if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import (cooperative)");
+        if (launched) {
+            t_last_step_path = KVOPS_STEP_COOP;
+            return KVOPS_OK;
+        }
+    }
+    bool remote = false;
+    if (sds != nullptr && path == KVOPS_STEP_FUSED && bulk_copy_ok(gp, &remote)) {
+        bool launched = false;
+        cudaError_t e = kvb::launch_sieve_import(sp, gp, st, &launched);
+        if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import");
+        if (launched) {
+            t_last_step_path = KVOPS_STEP_FUSED;
+            return KVOPS_OK;
+        }
+    }
+    t_last_step_path = KVOPS_STEP_SPLIT;
+    // The same step as two kernels (state too large for the fused kernel, host or unaligned rows).
+    if (sds != nullptr) {
+        cudaError_t e = kvb::launch_sieve_update(sp, st, sds->sm_count);
+        if (e != cudaSuccess) return cuda_fail(e, "launch hisp_sieve_update");
+    }
+    cudaError_t e = kvb::launch_gather(gp, st, ds->sm_count);
+    if (e != cudaSuccess) return cuda_fail(e, "launch kvc_gather_rows");
+    return KVOPS_OK;
+}
+
+uint32_t kvops_last_step_path(void) { return t_last_step_path; }
 
 int kvops_sieve_ht_init(uint64_t device_buffer_tokens, uint64_t device_buffer_ht, uint64_t prefill_lens,
                         uint32_t req_start, uint32_t num_reqs, uint32_t layer_num, uint32_t pool_size,

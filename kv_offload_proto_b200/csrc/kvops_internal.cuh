@@ -99,6 +99,15 @@ struct ExportParams {
     StatusTarget st;
 };
 
+// Extra arguments of the layer-step kernels (sieve.cu).
+struct StepExtra {
+    int32_t nsl;        // copy warp: sets of 32 ring slots
+    uint32_t ring_off;  // copy warp: byte offset of the ring in dynamic shared memory
+    uint32_t *flags;    // cooperative step: the launch's block of 256 ready words
+    uint32_t epoch;     // cooperative step: set in the kernel from the block (host passes 0)
+    uint32_t magic;     // copy helpers: multiply-high constant of cta_copy_rows (0: divide)
+};
+
 // Publishes completion: called by thread 0 of every CTA after a __syncthreads() that
 // follows the CTA's last data store. The last CTA to arrive writes
 // (1<<32)|err into each status word with system-scope release, then recycles the ticket.
@@ -140,5 +149,16 @@ cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int sm_cou
 cudaError_t launch_sieve_ht_init(const HtInitParams &p, cudaStream_t s);
 cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count);
 cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count);
+// Fused SIEVE step + miss-row gather (one CTA per request). Sets *launched = false, launching
+// nothing, when the request's state and the copy ring do not fit shared memory; the caller
+// then runs launch_sieve_update and launch_gather instead.
+cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cudaStream_t s, bool *launched);
+// The same step as one cooperative launch: the SIEVE CTAs publish their slots and miss flags
+// after the hand sweep (ready words in `flags`, a zero-initialised block of 256 words that no
+// other launch uses while this one runs) and every other CTA resident on the GPU copies miss
+// rows of ready requests. *launched = false (nothing launched) when fewer than 8 copy CTAs fit
+// beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
+                              bool *launched);
 
 }  // namespace kvb

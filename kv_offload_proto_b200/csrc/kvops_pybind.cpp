@@ -79,6 +79,29 @@ void import_multi(const std::vector<uint64_t> &seg_bases, uint32_t layer_offset_
                              status, stream, block_dim, &o));
 }
 
+void sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_lens, uint64_t prefill_lens,
+                  uint64_t device_buffer_tokens, uint64_t device_buffer_visited, uint64_t device_buffer_ht,
+                  uint64_t sieve_hand, uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real,
+                  uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size, uint32_t visited_stride_b,
+                  uint32_t max_num_reqs, uint32_t pool_size, const std::vector<uint64_t> &seg_bases,
+                  uint32_t layer_offset_rows, uint32_t per_layer_seg_rows, uint32_t row_bytes, uint64_t req_host_base,
+                  uint64_t hot_row_base, uint32_t stripe_rows, uint64_t status, uint64_t stream, uint32_t block_dim,
+                  uint64_t hot_req_stride_rows, bool injective, const std::string &path)
+{
+    KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    if (path == "auto") o.step_path = KVOPS_STEP_AUTO;
+    else if (path == "fused") o.step_path = KVOPS_STEP_FUSED;
+    else if (path == "split") o.step_path = KVOPS_STEP_SPLIT;
+    else if (path == "coop") o.step_path = KVOPS_STEP_COOP;
+    else throw std::invalid_argument("sieve_import: path must be 'auto', 'coop', 'fused' or 'split'");
+    check(kvops_sieve_import(topk_indices, req_pool_indices, seq_lens, prefill_lens, device_buffer_tokens,
+                             device_buffer_visited, device_buffer_ht, sieve_hand, topk_device_slots, is_miss, num_real,
+                             top_k, device_buffer_size, padded_buffer_size, visited_stride_b, max_num_reqs, pool_size,
+                             static_cast<uint32_t>(seg_bases.size()), seg_bases.data(), layer_offset_rows,
+                             per_layer_seg_rows, row_bytes, req_host_base, hot_row_base, stripe_rows, status, stream,
+                             block_dim, &o));
+}
+
 void export_seg_alllayer(uint64_t channel, uint64_t seg_base, uint32_t per_layer_seg_rows, uint32_t row_bytes,
                          uint32_t row_lo, uint32_t row_cnt, uint32_t layer_num, uint64_t src_layer0_base,
                          uint64_t src_layer_stride, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
@@ -167,6 +190,24 @@ PYBIND11_MODULE(_kvops, m)
           py::arg("num_real"), py::arg("top_k"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"),
           py::arg("visited_stride_b"), py::arg("max_num_reqs"), py::arg("pool_size"), py::arg("stream") = 0,
           py::arg("block_dim") = 8);
+    // One layer-step: sieve_update then import_multi, fused when possible (not in the reference module).
+    m.def("sieve_import", &sieve_import, py::arg("topk_indices"), py::arg("req_pool_indices"), py::arg("seq_lens"),
+          py::arg("prefill_lens"), py::arg("device_buffer_tokens"), py::arg("device_buffer_visited"),
+          py::arg("device_buffer_ht"), py::arg("sieve_hand"), py::arg("topk_device_slots"), py::arg("is_miss"),
+          py::arg("num_real"), py::arg("top_k"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"),
+          py::arg("visited_stride_b"), py::arg("max_num_reqs"), py::arg("pool_size"), py::arg("seg_bases"),
+          py::arg("layer_offset_rows"), py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("req_host_base"),
+          py::arg("hot_row_base"), py::arg("stripe_rows"), py::arg("status"), py::arg("stream") = 0,
+          py::arg("block_dim") = 1, py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false,
+          py::arg("path") = "auto");
+    m.def("last_step_path", []() {
+        switch (kvops_last_step_path()) {
+            case KVOPS_STEP_COOP: return std::string("coop");
+            case KVOPS_STEP_FUSED: return std::string("fused");
+            case KVOPS_STEP_SPLIT: return std::string("split");
+            default: return std::string("none");
+        }
+    });
     m.def("sieve_ht_init", &sieve_ht_init, py::arg("device_buffer_tokens"), py::arg("device_buffer_ht"),
           py::arg("prefill_lens"), py::arg("req_start"), py::arg("num_reqs"), py::arg("layer_num"),
           py::arg("pool_size"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"), py::arg("ht_size"),

@@ -6,55 +6,17 @@
 // position (or destination row) each, the accepted rows are appended to a shared list, and
 // the whole CTA then streams the list as one flat array of 16-byte chunks with 8 loads in
 // flight per thread before the matching stores. Sources may be own HBM, a peer GPU's HBM (UVA,
-// NVLink/NVSwitch) or pinned host memory; loads are plain (no TMA, no multicast).
+// NVLink/NVSwitch) or pinned host memory; every load is a plain global load.
 #include <stdint.h>
 
 #include "kvops_internal.cuh"
+#include "rows_common.cuh"
 
 namespace kvb {
 namespace {
 
 constexpr int kRowThreads = 256;
 constexpr int kUnroll = 8;
-
-template <typename V>
-__device__ __forceinline__ V load_stream(const V *p)
-{
-    return __ldcs(p);
-}
-template <>
-__device__ __forceinline__ uint8_t load_stream<uint8_t>(const uint8_t *p)
-{
-    return *reinterpret_cast<const volatile uint8_t *>(p);
-}
-
-// Copies n rows (src[i] -> dst[i]) of `row_bytes` with the whole CTA: the rows form one flat
-// array of V-sized chunks split evenly over the threads, kUnroll loads in flight per thread
-// before the matching stores. `magic` = ceil(2^32 / chunks_per_row) when exact division by
-// multiply-high is valid for every chunk index (host-checked), else 0.
-template <typename V>
-__device__ __forceinline__ void cta_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
-                                              uint32_t row_bytes, uint32_t magic)
-{
-    const uint32_t cpr = row_bytes / sizeof(V);
-    const uint32_t total = static_cast<uint32_t>(n) * cpr;
-    for (uint32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * kUnroll) {
-        V v[kUnroll];
-        uint32_t rr[kUnroll], cc[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const uint32_t i = i0 + u * blockDim.x;
-            const uint32_t r = magic ? __umulhi(i, magic) : i / cpr;
-            rr[u] = r;
-            cc[u] = i - r * cpr;
-            if (i < total) v[u] = load_stream(reinterpret_cast<const V *>(src[r]) + cc[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            if (i0 + u * blockDim.x < total) reinterpret_cast<V *>(dst[rr[u]])[cc[u]] = v[u];
-        }
-    }
-}
 
 // One tile = kGatherTile consecutive positions per CTA iteration: every thread evaluates one
 // position (kvc_gather_rows.cpp:54-76), the accepted rows are appended to a shared list, and
@@ -68,53 +30,19 @@ __global__ void __launch_bounds__(kRowThreads, 4) gather_kernel(const GatherPara
     __shared__ const uint8_t *s_src[kGatherTile];
     __shared__ uint8_t *s_dst[kGatherTile];
     __shared__ int s_n;
-    const int lane = threadIdx.x & 31;
+    // Launched as a programmatic dependent of the SIEVE step: the CTAs may start while that
+    // kernel runs and wait here for its completion (and memory flush) before reading its
+    // outputs. Without the launch attribute this returns at once.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
     int32_t num_real = p.num_real != nullptr ? *p.num_real : 0;
     if (num_real > static_cast<int32_t>(p.max_num_reqs)) num_real = static_cast<int32_t>(p.max_num_reqs);
     const int64_t total = num_real > 0 ? static_cast<int64_t>(num_real) * p.top_k : 0;
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * kGatherTile; base < total;
          base += static_cast<int64_t>(gridDim.x) * kGatherTile) {
-        if (threadIdx.x == 0) s_n = 0;
-        __syncthreads();
-        const int64_t pos = base + threadIdx.x;
-        bool ok = false;
-        const uint8_t *src = nullptr;
-        uint8_t *dst = nullptr;
-        if (pos < total && p.is_miss[pos] != 0) {  // kvc_gather_rows.cpp:55-57
-            const int32_t t = p.topk[pos];
-            const int32_t slot = p.slots[pos];
-            const int64_t bid = pos / p.top_k;
-            const int64_t req = p.req_pool[bid];
-            if (t >= 0 && slot >= 0 && req >= 0) {  // :62-68
-                const uint32_t row = static_cast<uint32_t>(p.host_base[bid] + t);
-                const uint32_t node = node_of(row, p.stripe, p.nodes);
-                if (p.my_node == kAllNodes || node == p.my_node) {  // :69-72
-                    const uint32_t seg_row = seg_row_of(row, p.stripe, p.nodes, p.injective != 0);
-                    const uint8_t *seg = node < static_cast<uint32_t>(kMaxNodes) ? p.seg[node] : nullptr;
-                    if (seg == nullptr) {
-                        record_error(p.st, KVOPS_ERR_SEG_NULL);
-                    } else if (seg_row >= p.plsr) {  // bounds check the reference lacks
-                        record_error(p.st, KVOPS_ERR_ROW_BASE + (static_cast<uint32_t>(pos) & 0xFFu) + (1u << 16));
-                    } else {
-                        src = seg + (p.layer_offset_rows + seg_row) * static_cast<uint64_t>(p.row_bytes);
-                        dst = p.hot + static_cast<uint64_t>(req) * p.hot_req_stride_bytes +
-                              static_cast<uint64_t>(slot) * p.row_bytes;  // :73-76
-                        ok = true;
-                    }
-                }
-            }
-        }
-        const unsigned mask = __ballot_sync(0xFFFFFFFFu, ok);
-        int at = 0;
-        if (lane == 0 && mask) at = atomicAdd(&s_n, __popc(mask));
-        at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(mask & ((1u << lane) - 1u));
-        if (ok) {
-            s_src[at] = src;
-            s_dst[at] = dst;
-        }
-        __syncthreads();
-        cta_copy_rows<V>(s_src, s_dst, s_n, p.row_bytes, magic);
-        __syncthreads();
+        const int64_t end = base + kGatherTile < total ? base + kGatherTile : total;
+        gather_tile<V, kUnroll, false>(p, base, end, s_src, s_dst, &s_n, magic);
     }
     __syncthreads();
     if (threadIdx.x == 0) arrive_and_publish(p.st);
@@ -189,7 +117,7 @@ __global__ void __launch_bounds__(kRowThreads, 4) export_kernel(const ExportPara
             s_dst[at] = dst;
         }
         __syncthreads();
-        cta_copy_rows<V>(s_src, s_dst, s_n, p.row_bytes, magic);
+        cta_copy_rows<V, kUnroll>(s_src, s_dst, s_n, p.row_bytes, magic);
         __syncthreads();
     }
     __syncthreads();
@@ -223,13 +151,24 @@ cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count)
     const uint64_t cpr = p.row_bytes / vb;
     const uint32_t magic = (cpr > 0 && cpr < 65536 && kGatherTile * cpr < 65536)
                                ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;
+    // Programmatic stream serialization: the CTAs launch as soon as the previous kernel (the
+    // SIEVE step, which triggers at entry) lets them, and gather_kernel waits for its completion.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kRowThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (vb) {
-        case 16: gather_kernel<uint4><<<grid, kRowThreads, 0, s>>>(p, magic); break;
-        case 8: gather_kernel<uint2><<<grid, kRowThreads, 0, s>>>(p, magic); break;
-        case 4: gather_kernel<uint32_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
-        default: gather_kernel<uint8_t><<<grid, kRowThreads, 0, s>>>(p, magic); break;
+        case 16: return cudaLaunchKernelEx(&cfg, gather_kernel<uint4>, p, magic);
+        case 8: return cudaLaunchKernelEx(&cfg, gather_kernel<uint2>, p, magic);
+        case 4: return cudaLaunchKernelEx(&cfg, gather_kernel<uint32_t>, p, magic);
+        default: return cudaLaunchKernelEx(&cfg, gather_kernel<uint8_t>, p, magic);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count)

@@ -10,7 +10,12 @@
 // and the persisted state (including the hash-table bytes) equal the reference kernel's.
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "kvops_internal.cuh"
+#include "rows_common.cuh"
 
 namespace kvb {
 namespace {
@@ -138,22 +143,27 @@ __device__ int32_t sieve_sequential(const int32_t *tp, int32_t K, int32_t *os, i
 }
 
 // Cooperative copy of `bytes` bytes using the widest access both pointers allow.
-__device__ __forceinline__ void coop_copy(void *dst, const void *src, size_t bytes)
+__device__ __forceinline__ void coop_copy_n(void *dst, const void *src, size_t bytes, unsigned tid, unsigned nt)
 {
     const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
     if (((a | bytes) & 15) == 0) {
         uint4 *d = static_cast<uint4 *>(dst);
         const uint4 *s = static_cast<const uint4 *>(src);
-        for (size_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+        for (size_t i = tid; i < bytes / 16; i += nt) d[i] = s[i];
     } else if (((a | bytes) & 3) == 0) {
         uint32_t *d = static_cast<uint32_t *>(dst);
         const uint32_t *s = static_cast<const uint32_t *>(src);
-        for (size_t i = threadIdx.x; i < bytes / 4; i += blockDim.x) d[i] = s[i];
+        for (size_t i = tid; i < bytes / 4; i += nt) d[i] = s[i];
     } else {
         uint8_t *d = static_cast<uint8_t *>(dst);
         const uint8_t *s = static_cast<const uint8_t *>(src);
-        for (size_t i = threadIdx.x; i < bytes; i += blockDim.x) d[i] = s[i];
+        for (size_t i = tid; i < bytes; i += nt) d[i] = s[i];
     }
+}
+
+__device__ __forceinline__ void coop_copy(void *dst, const void *src, size_t bytes)
+{
+    coop_copy_n(dst, src, bytes, threadIdx.x, blockDim.x);
 }
 
 // Asynchronous global -> shared staging: 16-byte cp.async when both sides allow it (all
@@ -207,6 +217,9 @@ __host__ __device__ __forceinline__ SmemLayout sieve_smem_layout(int32_t padded,
 template <bool kStaged>
 __global__ void __launch_bounds__(kSieveThreads) sieve_update_kernel(const SieveParams p)
 {
+    // Lets a programmatic dependent (the gather of this layer-step) launch its CTAs now; they
+    // wait for this grid's completion before reading its outputs.
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) unsigned char smem[];
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k;
@@ -335,6 +348,7 @@ __global__ void __launch_bounds__(kSieveThreads) sieve_ht_init_kernel(const HtIn
 // written back and is recomputed by the sequential path from the untouched global state.
 
 constexpr int kFastThreads = 512;
+
 constexpr uint16_t kNone16 = 0xFFFFu;
 constexpr uint16_t kDelMark = 0xFFFFu;   // table cell: deleted entry (entries are <= 65520)
 constexpr uint16_t kLeadMark = 0xFFFEu;  // table cell: first deleted entry of its probe run
@@ -620,9 +634,370 @@ __device__ void passed_bits(const uint32_t *vini, uint32_t *vfin, const uint32_t
     }
 }
 
-__global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const SieveParams p)
+// ==== Fused step: the miss rows are copied while the table passes run ====================
+//
+// sieve_fast_kernel<true> adds a 17th warp. All 17 warps run phases 0-3; the outputs
+// (slots, miss flags) are final there. The extra warp then copies the request's miss rows
+// (kvc_gather_rows.cpp:54-76, the same position rules and error codes as gather_kernel) while
+// the other 16 run phases 4-6 on named barrier 1. Rows move through a shared-memory ring by
+// bulk copies: global -> shared completing on an mbarrier, then shared -> global into the
+// hot row. Sources are own or peer HBM (the host checks the 16-byte alignment every bulk
+// copy needs and routes other cases to the two-kernel path). Every wait is bounded.
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
 {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Waits for the phase with the given parity to complete; false after ~2^22 polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
+{
+    for (uint32_t i = 0; i < (1u << 22); ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void *src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile(
+        "{\n\t.reg .u64 g;\n\t"
+        "cvta.to.global.u64 g, %1;\n\t"
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [g], %2, [%3];\n\t}" ::"r"(dst_smem),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src_smem, uint32_t bytes)
+{
+    asm volatile(
+        "{\n\t.reg .u64 g;\n\t"
+        "cvta.to.global.u64 g, %0;\n\t"
+        "cp.async.bulk.global.shared::cta.bulk_group [g], [%1], %2;\n\t"
+        "cp.async.bulk.commit_group;\n\t}" ::"l"(dst),
+        "r"(src_smem), "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+__device__ __forceinline__ void bulk_wait_all()
+{
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// The copy warp. The miss positions are listed in order, then moved in groups of 32 rows
+// (one per lane) through `nset` sets of 32 ring slots: group g loads into set g % nset while
+// group g - (nset - 1) is stored, so up to nset groups are in flight. One mbarrier per set,
+// armed by lane 0 with the group's byte count, keeps every wait warp-uniform.
+constexpr int kMaxSets = 4;
+
+__device__ void copy_miss_rows(const GatherParams &g, int32_t bid, int64_t req, const int32_t *topk,
+                               const int32_t *os, const int8_t *om, int32_t K, unsigned char *ring, uint64_t *bars,
+                               uint16_t *list, int32_t nset)
+{
+    const unsigned kAll = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rb = g.row_bytes;
+    int32_t n = 0;  // miss positions, in position order (kvc_gather_rows.cpp:55-57)
+    for (int32_t k0 = 0; k0 < K; k0 += 32) {
+        const int32_t k = k0 + lane;
+        const bool m = k < K && om[k] != 0;
+        const uint32_t bal = __ballot_sync(kAll, m);
+        if (m) list[n + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint16_t>(k);
+        n += __popc(bal);
+    }
+    const uint32_t ring0 = smem_u32(ring), bar0 = smem_u32(bars);
+    if (lane < nset) mbar_init(bar0 + 8u * lane, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    const int64_t base = g.host_base[bid];
+    const uint64_t pos0 = static_cast<uint64_t>(bid) * g.top_k;
+    const int32_t ngroups = (n + 31) / 32;
+    uint8_t *dsts[kMaxSets] = {nullptr, nullptr, nullptr, nullptr};  // this lane's row per set
+    bool alive = true;
+    for (int32_t gi = 0; gi < ngroups + nset - 1 && alive; ++gi) {
+        if (gi < ngroups) {  // load group gi into set gi % nset
+            const int32_t set = gi % nset;
+            bulk_wait_read_all();  // the stores of the set's previous group have read it
+            const int32_t i = gi * 32 + lane;
+            const uint8_t *src = nullptr;
+            uint8_t *dst = nullptr;
+            if (i < n) {
+                const int32_t k = list[i];
+                const int32_t t = topk[k];
+                const int32_t slot = os[k];
+                if (t >= 0 && slot >= 0 && req >= 0) {  // :62-68
+                    const uint32_t row = static_cast<uint32_t>(base + t);
+                    const uint32_t node = node_of(row, g.stripe, g.nodes);
+                    const uint32_t seg_row = seg_row_of(row, g.stripe, g.nodes, g.injective != 0);
+                    const uint8_t *seg = node < static_cast<uint32_t>(kMaxNodes) ? g.seg[node] : nullptr;
+                    if (seg == nullptr) {
+                        record_error(g.st, KVOPS_ERR_SEG_NULL);
+                    } else if (seg_row >= g.plsr) {  // bounds check the reference lacks
+                        record_error(g.st, KVOPS_ERR_ROW_BASE + (static_cast<uint32_t>(pos0 + k) & 0xFFu) + (1u << 16));
+                    } else {
+                        src = seg + (g.layer_offset_rows + seg_row) * static_cast<uint64_t>(rb);
+                        dst = g.hot + static_cast<uint64_t>(req) * g.hot_req_stride_bytes +
+                              static_cast<uint64_t>(slot) * rb;  // :73-76
+                    }
+                }
+            }
+            const uint32_t bal = __ballot_sync(kAll, dst != nullptr);
+            if (lane == 0) mbar_expect_tx(bar0 + 8u * set, static_cast<uint32_t>(__popc(bal)) * rb);
+            __syncwarp();
+            if (dst != nullptr) bulk_load(ring0 + static_cast<uint32_t>(set * 32 + lane) * rb, src, rb, bar0 + 8u * set);
+#pragma unroll
+            for (int q = 0; q < kMaxSets; ++q)
+                if (q == set) dsts[q] = dst;
+        }
+        const int32_t r = gi - (nset - 1);  // store group r
+        if (r >= 0) {
+            const int32_t set = r % nset;
+            if (!mbar_wait(bar0 + 8u * set, static_cast<uint32_t>(r / nset) & 1u)) {
+                if (lane == 0) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
+                alive = false;
+                break;
+            }
+            uint8_t *dst = nullptr;
+#pragma unroll
+            for (int q = 0; q < kMaxSets; ++q)
+                if (q == set) dst = dsts[q];
+            if (dst != nullptr) bulk_store(dst, ring0 + static_cast<uint32_t>(set * 32 + lane) * rb, rb);
+        }
+    }
+    bulk_wait_all();
+    __syncwarp();
+}
+
+// Compute-role barrier: the whole CTA, or with the copy warp split off, the 16 compute warps.
+template <bool kFused>
+__device__ __forceinline__ void compute_sync()
+{
+    if (kFused)
+        asm volatile("bar.sync 1, %0;" ::"r"(kFastThreads) : "memory");
+    else
+        __syncthreads();
+}
+
+// ---- cooperative layer-step: ready words and copy helpers ----
+
+// Publishes that request `bid`'s slots and miss flags are in global memory (after a barrier
+// that follows their stores).
+__device__ __forceinline__ void raise_ready(const StepExtra &x, int32_t bid)
+{
+    __threadfence();
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(x.flags + bid), "r"(x.epoch) : "memory");
+}
+
+// Waits for a ready word; false after ~2^24 polls (more than a second).
+__device__ __forceinline__ bool wait_ready(const uint32_t *f, uint32_t epoch)
+{
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v == epoch) return true;
+        __nanosleep(64);
+    }
+    return false;
+}
+
+// Layout of a launch's block of 256 ready words: [0, kMaxCoopReqs) one per request; copy items
+// are claimed with one atomicAdd on kClaimWord, which SIEVE CTA 0 zeroes at kernel entry before
+// it sets kClaimInit to the epoch (every CTA waits for that once before its first claim, so a
+// count left by an older launch is never used). The epoch itself lives on the device: every
+// CTA reads kEpochWord at entry and uses its value + 1; the last CTA to finish (kArriveWord)
+// stores that value back. A launch replayed from a CUDA graph therefore gets a new epoch each
+// time without any host work.
+constexpr int kClaimInit = 252, kClaimWord = 253, kArriveWord = 254, kEpochWord = 255, kMaxCoopReqs = 252;
+constexpr int kCoopUnroll = 12;  // 16-byte loads in flight per thread of a copy CTA
+
+__device__ __forceinline__ void init_claims(const StepExtra &x)
+{
+    *reinterpret_cast<volatile uint32_t *>(x.flags + kClaimWord) = 0u;
+    __threadfence();
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(x.flags + kClaimInit), "r"(x.epoch) : "memory");
+}
+
+// The next item index, or -1 if the claim counter was never initialised (not expected).
+__device__ __forceinline__ int64_t claim_item(const StepExtra &x, bool *inited)
+{
+    if (!*inited) {
+        if (!wait_ready(x.flags + kClaimInit, x.epoch)) return -1;
+        *inited = true;
+    }
+    return static_cast<int64_t>(atomicAdd(x.flags + kClaimWord, 1u));
+}
+
+// Called by thread 0 of every CTA of a cooperative step once the CTA has finished.
+__device__ __forceinline__ void finish_block(const StepExtra &x)
+{
+    __threadfence();
+    if (atomicAdd(x.flags + kArriveWord, 1u) != gridDim.x - 1) return;
+    *reinterpret_cast<volatile uint32_t *>(x.flags + kArriveWord) = 0u;
+    __threadfence();
+    *reinterpret_cast<volatile uint32_t *>(x.flags + kEpochWord) = x.epoch;
+    __threadfence();
+}
+
+__device__ __forceinline__ bool probe_ready(const uint32_t *f, uint32_t epoch)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v == epoch;
+}
+
+// Copies miss rows of ready requests until none are left: items are tiles of blockDim
+// positions in request order, claimed one at a time, gathered as gather_kernel does. The next
+// item's inputs are loaded before the current item's rows are copied (two row lists), so
+// their latency hides under the copy. Run by the copy CTAs from the start and by every SIEVE
+// CTA once its own step is written back.
+__device__ void copy_ready_rows(const SieveParams &p, const GatherParams &g, const StepExtra &x, unsigned char *smem)
+{
+    __shared__ int s_n[2];
+    __shared__ long long s_item;
+    __shared__ int s_state;  // next item probed: 1 ready, 0 not yet, -1 gave up waiting
+    __shared__ int s_late;   // the same after waiting (its own word: s_state may still be read)
+    const unsigned tid = threadIdx.x, nt = blockDim.x;
+    // row list c: sources at smem + 16*nt*c, destinations 8*nt bytes after them
+    auto srcs = [&](int c) { return reinterpret_cast<const uint8_t **>(smem + 16 * nt * c); };
+    auto dsts = [&](int c) { return reinterpret_cast<uint8_t **>(smem + 16 * nt * c + 8 * nt); };
+    int32_t num_real = *p.num_real;
+    if (num_real > p.max_num_reqs) num_real = p.max_num_reqs;
+    const int32_t K = p.top_k, tile = static_cast<int32_t>(nt);
+    const int32_t per_req = (K + tile - 1) / tile;
+    const int64_t items = static_cast<int64_t>(num_real > 0 ? num_real : 0) * per_req;
+    bool inited = false;  // meaningful in thread 0 only
+    auto range = [&](int64_t it, int64_t *lo, int64_t *hi, int32_t *r) {
+        *r = static_cast<int32_t>(it / per_req);
+        *lo = static_cast<int64_t>(*r) * K + (it % per_req) * tile;
+        const int64_t end = static_cast<int64_t>(*r + 1) * K;
+        *hi = *lo + tile < end ? *lo + tile : end;
+    };
+    if (tid == 0) {
+        s_n[0] = s_n[1] = 0;
+        const int64_t it = claim_item(x, &inited);
+        s_item = it;
+        s_state = 0;
+        if (it >= 0 && it < items) s_state = wait_ready(x.flags + it / per_req, x.epoch) ? 1 : -1;
+    }
+    __syncthreads();
+    int64_t cur = s_item;
+    if (cur < 0 || cur >= items) return;
+    {
+        int64_t lo, hi;
+        int32_t r;
+        range(cur, &lo, &hi, &r);
+        const uint8_t *src = nullptr;
+        uint8_t *dst = nullptr;
+        const bool ok = s_state == 1 && lo + tid < hi && gather_position<true>(g, lo + tid, &src, &dst);
+        list_append(ok, src, dst, srcs(0), dsts(0), &s_n[0]);
+        if (tid == 0 && s_state != 1) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
+    }
+    __syncthreads();
+    for (int c = 0;; c ^= 1) {
+        if (tid == 0) {
+            const int64_t it = claim_item(x, &inited);
+            s_item = it;
+            s_state = it >= 0 && it < items && probe_ready(x.flags + it / per_req, x.epoch) ? 1 : 0;
+        }
+        __syncthreads();
+        const int64_t nxt = s_item;
+        const bool valid = nxt >= 0 && nxt < items;
+        int state = s_state;
+        int64_t lo = 0, hi = 0;
+        int32_t r = 0;
+        if (valid) range(nxt, &lo, &hi, &r);
+        const int64_t pos = lo + tid;
+        int8_t miss = 0;
+        int32_t t = -1, slot = -1;
+        int64_t req = -1, base = 0;
+        if (state == 1 && pos < hi) {  // issued now, consumed after the copy below
+            miss = __ldcg(g.is_miss + pos);
+            t = g.topk[pos];
+            slot = __ldcg(g.slots + pos);
+            req = g.req_pool[r];
+            base = g.host_base[r];
+        }
+        cta_copy_rows<uint4, kCoopUnroll>(srcs(c), dsts(c), s_n[c], g.row_bytes, x.magic);
+        if (valid) {
+            if (state != 1) {
+                if (tid == 0) s_late = wait_ready(x.flags + r, x.epoch) ? 1 : -1;
+                __syncthreads();
+                state = s_late;
+                if (state == 1 && pos < hi) {
+                    miss = __ldcg(g.is_miss + pos);
+                    t = g.topk[pos];
+                    slot = __ldcg(g.slots + pos);
+                    req = g.req_pool[r];
+                    base = g.host_base[r];
+                }
+                if (tid == 0 && state != 1) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
+            }
+            const uint8_t *src = nullptr;
+            uint8_t *dst = nullptr;
+            const bool ok = state == 1 && pos < hi && gather_eval(g, pos, miss, t, slot, req, base, &src, &dst);
+            list_append(ok, src, dst, srcs(c ^ 1), dsts(c ^ 1), &s_n[c ^ 1]);
+        }
+        __syncthreads();
+        if (!valid) break;
+        if (tid == 0) s_n[c] = 0;
+    }
+}
+
+// kMode 0: SIEVE step only (hisp_sieve_update). 1: plus a copy warp that moves the miss rows
+// during phases 4-6. 2: cooperative launch with copy helper CTAs after the SIEVE CTAs.
+template <int kMode>
+__global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
+    sieve_fast_kernel(const SieveParams p, const GatherParams g, const StepExtra x0)
+{
+    constexpr bool kFused = kMode == 1;  // the copy warp splits off after phase 3
+    // Lets a programmatic dependent (the gather of this layer-step) launch its CTAs now; they
+    // wait for this grid's completion before reading its outputs.
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ uint32_t s_epoch;
+    StepExtra x = x0;
+    if (kMode == 2) {
+        if (threadIdx.x == 0) {
+            s_epoch = *reinterpret_cast<volatile const uint32_t *>(x0.flags + kEpochWord) + 1u;
+            if (blockIdx.x == 0) {
+                x.epoch = s_epoch;
+                init_claims(x);
+            }
+        }
+        __syncthreads();
+        x.epoch = s_epoch;
+    }
+    if (kMode == 2 && static_cast<int32_t>(blockIdx.x) >= p.max_num_reqs) {  // a copy CTA
+        copy_ready_rows(p, g, x, smem);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            arrive_and_publish(g.st);
+            finish_block(x);
+        }
+        return;
+    }
     __shared__ int s_flag;     // nonzero: recompute this step with the sequential path
     __shared__ int s_changed[2];  // per-round progress flags, used alternately
     __shared__ int s_any_miss;
@@ -641,6 +1016,18 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     const int64_t req = bid < num_real ? p.req_pool[bid] : -1;
     if (bid >= num_real || req < 0 || req >= p.pool_size) {  // :72-88
         fill_dummy(g_slots, g_miss, K);
+        if (kMode != 0) {  // no rows to copy (all miss flags 0); the CTA still completes the status
+            __syncthreads();
+            if (kMode == 2) {
+                if (tid == 0) raise_ready(x, bid);
+                copy_ready_rows(p, g, x, smem);
+                __syncthreads();
+            }
+            if (tid == 0) {
+                arrive_and_publish(g.st);
+                if (kMode == 2) finish_block(x);
+            }
+        }
         return;
     }
     const int32_t seq_len = p.seq_lens[bid];
@@ -832,10 +1219,36 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
     }
     __syncthreads();
 
+    if (kFused && tid >= kFastThreads) {  // the copy warp
+        const int32_t nsl = x.nsl;
+        unsigned char *ring = smem + x.ring_off;
+        uint64_t *bars = reinterpret_cast<uint64_t *>(ring + static_cast<size_t>(32 * nsl) * g.row_bytes);
+        uint16_t *list = reinterpret_cast<uint16_t *>(bars + kMaxSets);
+        // Outputs are final now unless the step already fell back; then copy after the
+        // sequential path. (A fallback raised later, by the insert-round bound, rewrites each
+        // output once with the value already there: phases 2-3 verified them.)
+        const bool early = !s_flag;
+        if (early) copy_miss_rows(g, bid, req, s_topk, s_os, s_om, K, ring, bars, list, nsl);
+        __syncthreads();  // the compute warps have finished the step
+        if (!early) copy_miss_rows(g, bid, req, s_topk, s_os, s_om, K, ring, bars, list, nsl);
+        if ((tid & 31) == 0) arrive_and_publish(g.st);
+        return;
+    }
+    const int ntc = kFused ? kFastThreads : nt;  // threads of the compute role
+    // Cooperative step: the outputs are final now (unless the step already fell back), so
+    // publish them for the copy helpers before the table passes.
+    const bool raised = kMode == 2 && !s_flag;
+    if (raised) {
+        coop_copy(g_slots, s_os, 4ull * K);
+        coop_copy(g_miss, s_om, static_cast<size_t>(K));
+        __syncthreads();
+        if (tid == 0) raise_ready(x, bid);
+    }
+
     // ---- phase 4: delete the evicted tokens from the table, re-packing each probe run ----
     const bool update_table = !s_flag && s_any_miss;
     if (update_table) {
-        for (int32_t c = tid; c < dbs; c += nt) {
+        for (int32_t c = tid; c < dbs; c += ntc) {
             if (s_evt[c] == kNone16 || s_tok[c] < 0) continue;
             uint32_t idx = ht_hash(s_tok[c]) & mask;
             for (uint32_t n = 0; n <= mask; ++n) {
@@ -847,9 +1260,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             }
         }
     }
-    __syncthreads();
+    compute_sync<kFused>();
     if (update_table) {  // the first deleted cell of each run leads its re-pack
-        for (uint32_t i = tid; i <= mask; i += nt) {
+        for (uint32_t i = tid; i <= mask; i += ntc) {
             if (s_ht[i] != kDelMark) continue;
             uint32_t j = (i - 1) & mask;
             bool lead = true;
@@ -865,9 +1278,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             if (lead) s_ht[i] = kLeadMark;
         }
     }
-    __syncthreads();
+    compute_sync<kFused>();
     if (update_table) {
-        for (uint32_t i = tid; i <= mask; i += nt) {
+        for (uint32_t i = tid; i <= mask; i += ntc) {
             if (s_ht[i] != kLeadMark) continue;
             // Walk the run from its first deleted cell; every surviving entry moves to the
             // first empty cell from its home, which is never past its old cell.
@@ -885,14 +1298,14 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             }
         }
     }
-    __syncthreads();
+    compute_sync<kFused>();
 
     // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
     uint16_t *s_keys = reinterpret_cast<uint16_t *>(smem + L.dkey);  // candidate list no longer needed
     if (update_table) {
         if (tid == 0) s_nkeys = 0;
-        __syncthreads();
-        for (int32_t m0 = 0; m0 < K; m0 += nt) {  // list the misses (warp-aggregated appends)
+        compute_sync<kFused>();
+        for (int32_t m0 = 0; m0 < K; m0 += ntc) {  // list the misses (warp-aggregated appends)
             const int32_t m = m0 + tid;
             const bool is_key = m < K && ((s_missb[m >> 5] >> (m & 31)) & 1u);
             const unsigned bal = __ballot_sync(0xFFFFFFFFu, is_key);
@@ -906,7 +1319,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             }
         }
     }
-    __syncthreads();
+    compute_sync<kFused>();
     if (update_table) {
         const int32_t nkeys = s_nkeys;
         const int32_t limit = 4 * p.ht_size + 64;
@@ -914,7 +1327,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
             // Round r raises s_changed[r & 1]; thread 0 clears the other flag once every thread
             // has passed the first barrier of round r, i.e. after all reads of round r-1's flag.
             bool ch = false;
-            for (int32_t j = tid; j < nkeys; j += nt) {
+            for (int32_t j = tid; j < nkeys; j += ntc) {
                 const int32_t m = s_keys[j];
                 if (s_cls[m] != kClsPending) continue;
                 const uint16_t entry = static_cast<uint16_t>(s_os[m] + 1);
@@ -934,9 +1347,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
                     }
                 }
             }
-            __syncthreads();
+            compute_sync<kFused>();
             if (tid == 0) s_changed[(round + 1) & 1] = 0;
-            for (int32_t j = tid; j < nkeys; j += nt) {
+            for (int32_t j = tid; j < nkeys; j += ntc) {
                 const int32_t m = s_keys[j];
                 if (s_cls[m] == kClsPlaced && s_ht[s_aux[m]] != static_cast<uint16_t>(s_os[m] + 1)) {
                     s_cls[m] = kClsPending;
@@ -945,34 +1358,46 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
                 }
             }
             if (ch) s_changed[round & 1] = 1;
-            __syncthreads();
+            compute_sync<kFused>();
             if (!s_changed[round & 1]) break;
             if (round > limit) {  // cannot happen on a table at load <= 0.5; recompute if it does
                 if (tid == 0) s_flag = 1;
-                __syncthreads();
+                compute_sync<kFused>();
                 break;
             }
         }
     }
-    __syncthreads();
+    compute_sync<kFused>();
 
     if (!s_flag) {
         // ---- phase 6: write back ----
-        for (int32_t m = tid; m < K; m += nt)
+        for (int32_t m = tid; m < K; m += ntc)
             if ((s_missb[m >> 5] >> (m & 31)) & 1u) g_tok[s_os[m]] = s_topk[m];
-        coop_copy(g_slots, s_os, 4ull * K);
-        coop_copy(g_miss, s_om, static_cast<size_t>(K));
-        coop_copy(g_vis, s_vfin, p.vis_stride);
-        if (s_any_miss) coop_copy(g_ht, s_ht, 2ull * p.ht_size);
+        if (!raised) {
+            coop_copy_n(g_slots, s_os, 4ull * K, tid, ntc);
+            coop_copy_n(g_miss, s_om, static_cast<size_t>(K), tid, ntc);
+        }
+        coop_copy_n(g_vis, s_vfin, p.vis_stride, tid, ntc);
+        if (s_any_miss) coop_copy_n(g_ht, s_ht, 2ull * p.ht_size, tid, ntc);
         if (tid == 0) *g_hand = s_hand;
+        if (kFused) __syncthreads();  // meets the copy warp
+        if (kMode == 2) {  // the step is written back: help copy, then complete the status
+            __syncthreads();
+            copy_ready_rows(p, g, x, smem);
+            __syncthreads();
+            if (tid == 0) {
+                arrive_and_publish(g.st);
+                finish_block(x);
+            }
+        }
         return;
     }
 
     // ---- exact sequential path from the untouched global state ----
-    coop_copy(s_ht, g_ht, 2ull * p.ht_size);
-    coop_copy(s_tok, g_tok, 4ull * padded);
-    coop_copy(s_vfin, g_vis, p.vis_stride);
-    __syncthreads();
+    coop_copy_n(s_ht, g_ht, 2ull * p.ht_size, tid, ntc);
+    coop_copy_n(s_tok, g_tok, 4ull * padded, tid, ntc);
+    coop_copy_n(s_vfin, g_vis, p.vis_stride, tid, ntc);
+    compute_sync<kFused>();
     if (tid == 0) {
         int32_t hand = *g_hand;
         if (hand < 0 || hand >= dbs) hand = 0;
@@ -981,15 +1406,26 @@ __global__ void __launch_bounds__(kFastThreads, 1) sieve_fast_kernel(const Sieve
                                   padded, seq_len, prefill, hand, &dirty);
         s_dirty = dirty;
     }
-    __syncthreads();
-    coop_copy(g_slots, s_os, 4ull * K);
-    coop_copy(g_miss, s_om, static_cast<size_t>(K));
-    coop_copy(g_vis, s_vfin, p.vis_stride);
+    compute_sync<kFused>();
+    coop_copy_n(g_slots, s_os, 4ull * K, tid, ntc);
+    coop_copy_n(g_miss, s_om, static_cast<size_t>(K), tid, ntc);
+    coop_copy_n(g_vis, s_vfin, p.vis_stride, tid, ntc);
     if (s_dirty) {
-        coop_copy(g_tok, s_tok, 4ull * padded);
-        coop_copy(g_ht, s_ht, 2ull * p.ht_size);
+        coop_copy_n(g_tok, s_tok, 4ull * padded, tid, ntc);
+        coop_copy_n(g_ht, s_ht, 2ull * p.ht_size, tid, ntc);
     }
     if (tid == 0) *g_hand = s_hand;
+    if (kFused) __syncthreads();  // meets the copy warp
+    if (kMode == 2) {  // a fallback raised later rewrote the published outputs with equal values
+        __syncthreads();
+        if (tid == 0 && !raised) raise_ready(x, bid);
+        copy_ready_rows(p, g, x, smem);
+        __syncthreads();
+        if (tid == 0) {
+            arrive_and_publish(g.st);
+            finish_block(x);
+        }
+    }
 }
 
 int max_optin_smem()
@@ -1010,10 +1446,10 @@ cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int /*sm_c
     if (p.top_k <= 65535 && p.ht_size <= 65536 && p.dbs <= 65535) {
         const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
         if (F.total <= static_cast<size_t>(limit)) {
-            cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(F.total));
             if (e != cudaSuccess) return e;
-            sieve_fast_kernel<<<p.max_num_reqs, kFastThreads, F.total, s>>>(p);
+            sieve_fast_kernel<0><<<p.max_num_reqs, kFastThreads, F.total, s>>>(p, GatherParams{}, StepExtra{});
             return cudaGetLastError();
         }
     }
@@ -1027,6 +1463,93 @@ cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int /*sm_c
         sieve_update_kernel<false><<<p.max_num_reqs, 32, 0, s>>>(p);
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cudaStream_t s, bool *launched)
+{
+    *launched = false;
+    if (p.max_num_reqs <= 0 || p.top_k <= 0) return cudaSuccess;
+    if (p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return cudaSuccess;
+    const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
+    const size_t ring_off = align_up(F.total, 128);
+    const size_t limit = static_cast<size_t>(max_optin_smem());
+    for (int32_t nsl = kMaxSets; nsl >= 1; --nsl) {  // sets of 32 ring slots for the copy warp
+        const size_t total = ring_off + static_cast<size_t>(32 * nsl) * g.row_bytes + 8u * kMaxSets +
+                             2ull * static_cast<size_t>(p.top_k);
+        if (total > limit) continue;
+        cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(total));
+        if (e != cudaSuccess) return e;
+        StepExtra x{};
+        x.nsl = nsl;
+        x.ring_off = static_cast<uint32_t>(ring_off);
+        sieve_fast_kernel<1><<<p.max_num_reqs, kFastThreads + 32, total, s>>>(p, g, x);
+        *launched = true;
+        return cudaGetLastError();
+    }
+    return cudaSuccess;
+}
+
+// CTAs of sieve_fast_kernel<2> resident at once with `smem` bytes each (0 if it does not fit),
+// cached per device and size. The kernel's shared-memory limit only ever rises (to the largest
+// size used on the device), so every cached size stays launchable.
+cudaError_t coop_residency(size_t smem, int *resident)
+{
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> cache;
+    static std::map<int, size_t> limit_set;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({dev, smem});
+    if (it != cache.end()) {
+        *resident = it->second;
+        return cudaSuccess;
+    }
+    int n = 0;
+    if (smem <= static_cast<size_t>(max_optin_smem())) {
+        if (smem > limit_set[dev]) {
+            e = cudaFuncSetAttribute(sieve_fast_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            limit_set[dev] = smem;
+        }
+        int sms = 0, per_sm = 0;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sieve_fast_kernel<2>, kFastThreads, smem);
+        if (e != cudaSuccess) return e;
+        n = per_sm * sms;
+    }
+    cache[{dev, smem}] = n;
+    *resident = n;
+    return cudaSuccess;
+}
+
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
+                              bool *launched)
+{
+    *launched = false;
+    if (p.max_num_reqs <= 0 || p.top_k <= 0 || p.max_num_reqs > kMaxCoopReqs) return cudaSuccess;
+    if (p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return cudaSuccess;
+    const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
+    const size_t list = 4ull * sizeof(void *) * kFastThreads;  // two row lists of copy_ready_rows
+    const size_t total = F.total > list ? F.total : list;
+    int resident = 0;
+    cudaError_t e = coop_residency(total, &resident);
+    if (e != cudaSuccess) return e;
+    if (resident - p.max_num_reqs < 8) return cudaSuccess;
+    StepExtra x{};
+    x.flags = flags;
+    const uint32_t cpr = g.row_bytes / 16;  // helpers copy 16-byte chunks (host-checked)
+    x.magic = (cpr > 0 && cpr < 65536 && static_cast<uint64_t>(kFastThreads) * cpr < 65536)
+                  ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;
+    void *args[] = {const_cast<SieveParams *>(&p), const_cast<GatherParams *>(&g), &x};
+    e = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(sieve_fast_kernel<2>), dim3(resident),
+                                    dim3(kFastThreads), args, total, s);
+    if (e != cudaSuccess) return e;
+    *launched = true;
+    return cudaSuccess;
 }
 
 cudaError_t launch_sieve_ht_init(const HtInitParams &p, cudaStream_t s)

@@ -191,6 +191,31 @@ class DevicePool:
                                    block_dim, hot_req_stride_rows=hot_req_stride_rows, injective=self.injective)
         return status
 
+    def sieve_and_read(self, coord, layer_id, topk_indices, hot_row_base, stream=0, block_dim=1, *,
+                       hot_req_stride_rows=0, path="auto", publish=True) -> int:
+        """One decode layer-step in one call: `coord.sieve_update(layer_id, topk_indices)`
+        followed by `batch_read` of its miss rows from every segment (the reference driver's
+        pair, xds_decode.py:225-233), with identical results (kvops_sieve_import). path="auto"
+        runs one kernel that copies each request's miss rows during its table update when a
+        segment is on another GPU, and the two kernels (the gather launched as a programmatic
+        dependent) otherwise; "coop" / "fused" / "split" force one. Returns the status address for
+        `wait`, or 0 with publish=False: then no status words are written and completion is
+        observed on the stream (the form a CUDA graph can replay, see graph.StepGraph)."""
+        import torch
+        if topk_indices.dtype != torch.int32:
+            raise ValueError("topk_indices must be int32")
+        status = self.next_status() if publish else 0
+        self._k.sieve_import(
+            _ptr(topk_indices), _ptr(coord._req_pool_indices), _ptr(coord._seq_lens), _ptr(coord.prefill_lens),
+            _ptr(coord.device_buffer_tokens[layer_id]), _ptr(coord.device_buffer_visited[layer_id]),
+            _ptr(coord.device_buffer_ht[layer_id]), _ptr(coord.sieve_hand[layer_id]), _ptr(coord.top_k_device_slots),
+            _ptr(coord.is_miss), _ptr(coord.num_real), coord.top_k, coord.device_buffer_size,
+            coord.padded_buffer_size, coord.visited_stride_b, coord.max_num_reqs, coord.pool_size, self.seg_bases,
+            layer_id * self.per_layer_seg_rows, self.per_layer_seg_rows, self.row_bytes, _ptr(coord.req_host_base),
+            _ptr(hot_row_base), self.stripe_rows, status, stream, block_dim, hot_req_stride_rows=hot_req_stride_rows,
+            injective=self.injective, path=path)
+        return status
+
     def batch_write_alllayers(self, row_lo, row_cnt, src_layer0_base, src_layer_stride, stream=0, block_dim=1) -> int:
         """Export rows [row_lo, row_lo+row_cnt) of every layer to their segments
         (xds_ems_pool.py:220-230): one launch per segment, as in the reference."""

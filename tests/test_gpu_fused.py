@@ -1,0 +1,251 @@
+"""GPU parity of the fused layer-step (kvops_sieve_import, DevicePool.sieve_and_read): on twin
+copies of the same state and inputs it must equal the two-call path (sieve_update then
+import_multi) byte for byte — slots, miss flags, SIEVE state, hot rows, status words — and
+the SIEVE outputs, state and hot rows must equal the C restatement."""
+import numpy as np
+import pytest
+
+import oracle
+from gpu_util import config_topk, dev, host, host_view, kv
+
+pytestmark = pytest.mark.gpu
+
+
+class Side:
+    """One device copy of the SIEVE state (one layer slice used), hot buffer and status slots."""
+
+    def __init__(self, mod, st, hot_h, N):
+        self.tokens = dev(st.tokens)
+        self.visited = dev(st.visited)
+        self.ht = dev(st.ht.view(np.int16))
+        self.hand = dev(st.hand)
+        self.hot = dev(hot_h)
+        self.status = mod.alloc_status(8 * N)
+
+    def words(self, N, block_dim):
+        h = host_view(self.status, 8 * N * 64).view(np.uint64)
+        return np.array([[h[s * 8 + b] for b in range(block_dim)] for s in range(N)], np.uint64)
+
+
+def run_twins(seed=0, R=8, K=512, ctx=4096, dbs=1024, N=1, S=1, injective=False, row_bytes=1152, steps=3,
+              miss=0.2, block_dim=1, num_real=None, bad_req=False, ext=16, invalid=0.01, dup=0.01, corrupt=False,
+              segs_on_host=False, null_seg=None, plsr_cut=None, stride=True, layers=2, layer=1, path="coop",
+              expect=None):
+    import torch
+    mod = kv()
+    rng = np.random.default_rng(seed)
+    st = oracle.SieveState(layers, R, dbs, K)
+    for r in range(R):
+        st.admit(r, ctx)
+    if corrupt:  # slot 5 repeats slot 2's token without a table entry: the fast path must fall back
+        st.tokens[layer, :, 5] = st.tokens[layer, :, 2]
+    layer_rows = R * ctx
+    plsr = oracle.per_layer_seg_rows_injective(layer_rows, S, N) if (injective and S) else \
+        oracle.per_layer_seg_rows(layer_rows, N)
+    seg_bytes = layers * plsr * row_bytes
+    segs_h = [rng.integers(0, 256, seg_bytes, dtype=np.uint8) for _ in range(N)]
+    if segs_on_host:
+        addrs = [mod.segment_alloc(-1, seg_bytes) for _ in range(N)]
+        for a, h in zip(addrs, segs_h):
+            host_view(a, seg_bytes)[:] = h
+        keep = []
+    else:
+        keep = [dev(h) for h in segs_h]
+        addrs = [t.data_ptr() for t in keep]
+    if null_seg is not None:
+        addrs[null_seg] = 0
+    kplsr = plsr if plsr_cut is None else plsr_cut
+    hot_rows = R * dbs if stride else dbs
+    hot_h = rng.integers(0, 256, hot_rows * row_bytes, dtype=np.uint8)
+    a, b = Side(mod, st, hot_h, N), Side(mod, st, hot_h, N)
+    req_pool = np.arange(R, dtype=np.int64)
+    if bad_req:
+        req_pool[1] = -1
+    host_base = np.arange(R, dtype=np.int64) * ctx
+    nr = R if num_real is None else num_real
+    t_pool, t_base, t_nr = dev(req_pool), dev(host_base), dev(np.array([nr], np.int32))
+    prefill = dev(st.prefill_lens)
+    hs = dbs if stride else 0
+    exp_hot = hot_h.copy()
+    total_err = []
+    for step in range(steps):
+        topk = config_topk(rng, st, layer, req_pool, K, miss, ext=ext, invalid=invalid, dup=dup)
+        seq = np.full(R, ctx + ext, np.int32)
+        t_topk, t_seq = dev(topk), dev(seq)
+        out = []
+        for side, fused in ((a, False), (b, True)):
+            slots = torch.full((R, K), 7777, dtype=torch.int32, device="cuda")
+            missf = torch.full((R, K), 9, dtype=torch.int8, device="cuda")
+            sieve = (t_topk.data_ptr(), t_pool.data_ptr(), t_seq.data_ptr(), prefill.data_ptr(),
+                     side.tokens[layer].data_ptr(), side.visited[layer].data_ptr(), side.ht[layer].data_ptr(),
+                     side.hand[layer].data_ptr(), slots.data_ptr(), missf.data_ptr(), t_nr.data_ptr(), K, dbs,
+                     st.padded, st.vis_stride, R, R)
+            if fused:
+                mod.sieve_import(*sieve, addrs, layer * kplsr, kplsr, row_bytes, t_base.data_ptr(),
+                                 side.hot.data_ptr(), S, side.status, 0, block_dim, hot_req_stride_rows=hs,
+                                 injective=injective, path=path)
+                ran = mod.last_step_path()
+                assert ran == (expect or (path if path != "auto" else "coop")), ran
+            else:
+                mod.sieve_update(*sieve, 0, 8)
+                mod.import_multi(addrs, layer * kplsr, kplsr, row_bytes, t_topk.data_ptr(), t_pool.data_ptr(),
+                                 t_base.data_ptr(), slots.data_ptr(), missf.data_ptr(), t_nr.data_ptr(),
+                                 side.hot.data_ptr(), K, R, S, side.status, 0, block_dim, hot_req_stride_rows=hs,
+                                 injective=injective)
+            rcs = [mod.poll_status(side.status + s * 64 + q * 8, 10_000_000) for s in range(N)
+                   for q in range(block_dim)]
+            torch.cuda.synchronize()
+            out.append((host(slots), host(missf), rcs, side.words(N, block_dim)))
+        (sa, ma, ra, wa), (sb, mb, rb, wb) = out
+        np.testing.assert_array_equal(sb, sa)
+        np.testing.assert_array_equal(mb, ma)
+        for x, y in ((b.tokens, a.tokens), (b.visited, a.visited), (b.ht, a.ht), (b.hand, a.hand)):
+            np.testing.assert_array_equal(host(x), host(y))
+        exp_slots, exp_miss = st.update(layer, topk, req_pool, seq, num_real=nr)
+        np.testing.assert_array_equal(sb, exp_slots)
+        np.testing.assert_array_equal(mb, exp_miss)
+        np.testing.assert_array_equal(host(b.tokens)[layer], st.tokens[layer])
+        np.testing.assert_array_equal(host(b.visited)[layer], st.visited[layer])
+        np.testing.assert_array_equal(host(b.ht).view(np.uint16)[layer], st.ht[layer])
+        np.testing.assert_array_equal(host(b.hand)[layer][..., 0], st.hand[layer][..., 0])
+        # status: every word published; the same errCode (exact, or the same band for row errors)
+        assert (wa >> np.uint64(32) == 1).all() and (wb >> np.uint64(32) == 1).all()
+        ea, eb = int(wa[0, 0]) & 0xFFFFFFFF, int(wb[0, 0]) & 0xFFFFFFFF
+        assert (ea & ~0xFF) == (eb & ~0xFF) and (ea == eb or (ea & ~0xFF) == 0x10200), (hex(ea), hex(eb))
+        assert ra == [ea] * len(ra) and rb == [eb] * len(rb)
+        total_err.append(eb)
+        np.testing.assert_array_equal(host(b.hot), host(a.hot))
+        if null_seg is None and plsr_cut is None:
+            oracle.gather_all(segs_h, layer * plsr, row_bytes, topk, req_pool, host_base, exp_slots, exp_miss, nr,
+                              exp_hot, K, R, S, hs, injective)
+            np.testing.assert_array_equal(host(b.hot), exp_hot)
+    if segs_on_host:
+        for x in addrs:
+            mod.segment_free(x)
+    del keep
+    return total_err
+
+
+PATHS = ["coop", "fused"]  # cooperative copy CTAs; copy warp with bulk copies
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("row_bytes", [1152, 2048, 4096, 16384])
+def test_fused_matches_split_and_oracle(row_bytes, path):
+    # copy-warp ring: 4 .. 1 sets of 32 rows; 32 rows of 16 KB do not fit shared memory (two kernels)
+    expect = "split" if (path == "fused" and row_bytes == 16384) else None
+    assert run_twins(row_bytes=row_bytes, path=path, expect=expect) == [0, 0, 0]
+
+
+@pytest.mark.parametrize("path", ["auto", "split"])
+def test_sieve_import_other_paths(path):
+    assert run_twins(path=path, seed=21) == [0, 0, 0]
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("N,S,injective", [(3, 2, False), (3, 2, True), (1, 0, False)])
+def test_fused_striped_over_nodes(N, S, injective, path):
+    assert run_twins(N=N, S=S, injective=injective, block_dim=2, seed=3, path=path) == [0, 0, 0]
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_step_that_falls_back_to_sequential(path):
+    run_twins(corrupt=True, seed=5, path=path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_num_real_and_request_without_pool_row(path):
+    run_twins(num_real=6, bad_req=True, seed=7, path=path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("K", [20, 300])
+def test_fused_small_and_ragged_topk(K, path):
+    run_twins(K=K, seed=K, path=path)
+
+
+def test_pinned_host_segments():
+    """Plain-load copy helpers read host memory; the bulk-copy warp does not (two kernels)."""
+    run_twins(segs_on_host=True, N=2, S=1, steps=2, seed=9, path="coop")
+    run_twins(segs_on_host=True, N=2, S=1, steps=2, seed=9, path="fused", expect="split")
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_null_segment_reports_init_band(path):
+    errs = run_twins(N=2, S=1, null_seg=1, steps=2, seed=11, path=path)
+    assert errs == [0x101, 0x101]
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_row_outside_segment_reports_row_band(path):
+    errs = run_twins(plsr_cut=8 * 4096 // 2, steps=2, seed=13, path=path)
+    assert all((e & ~0xFF) == 0x10200 for e in errs)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_shared_hot_rows_single_request(path):
+    run_twins(R=1, stride=False, seed=15, path=path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_fused_config2_shape(path):
+    run_twins(R=64, K=2048, ctx=8192, dbs=4096, steps=3, miss=0.2, seed=1, path=path)
+
+
+def test_coop_too_many_requests_takes_two_kernels():
+    """More SIEVE CTAs than the ready-word block holds: the step runs as two kernels."""
+    run_twins(R=300, K=64, ctx=512, dbs=128, steps=2, seed=17, path="coop", expect="split")
+
+
+def test_sieve_and_read_equals_sieve_update_then_batch_read():
+    """The public API pair against the one-call method, through the coordinator and pool."""
+    import torch
+    from kv_offload_proto_b200.offload import XdsOffloadCoordinator
+    from kv_offload_proto_b200.pool import DevicePool, device_view
+    from kv_offload_proto_b200.workload import sample_topk_device
+    kv()
+    R, ctx, K, dbs, L = 16, 2048, 256, 512, 2
+    cos, pools, hots = [], [], []
+    for _ in range(2):
+        co = XdsOffloadCoordinator("cuda:0", L, R, dbs, K, R, ctx)
+        co.admit_all([ctx] * R, [r * ctx for r in range(R)])
+        co.set_batch(torch.arange(R, dtype=torch.int64, device="cuda"),
+                     torch.full((R,), ctx, dtype=torch.int32, device="cuda"))
+        pool = DevicePool(0, L, R * ctx, 1152, 1, segment_devices=(0, 0))
+        for s in range(2):
+            v = torch.as_tensor(np.arange(pool.segment_bytes // 4, dtype=np.int32) * (s + 1)).cuda()
+            device_view(pool.seg_bases[s], pool.segment_bytes, "cuda:0").copy_(v.view(torch.uint8))
+        cos.append(co)
+        pools.append(pool)
+        hots.append(torch.zeros((R * dbs * 1152,), dtype=torch.uint8, device="cuda"))
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    for step in range(3):
+        for layer in range(L):
+            topk = sample_topk_device(cos[0].device_buffer_tokens[layer, :R], ctx, dbs, K, 0.25, gen)
+            co, pool = cos[0], pools[0]
+            co.sieve_update(layer, topk)
+            st = pool.batch_read(layer, topk, co._req_pool_indices, co.req_host_base, co.top_k_device_slots,
+                                 co.is_miss, co.num_real, hots[0], R, K, 0, 1, hot_req_stride_rows=dbs)
+            pool.wait(st)
+            st = pools[1].sieve_and_read(cos[1], layer, topk, hots[1], 0, 1, hot_req_stride_rows=dbs)
+            pools[1].wait(st)
+            torch.cuda.synchronize()
+            assert torch.equal(cos[0].top_k_device_slots, cos[1].top_k_device_slots)
+            assert torch.equal(cos[0].is_miss, cos[1].is_miss)
+            for name in ("device_buffer_tokens", "device_buffer_visited", "device_buffer_ht", "sieve_hand"):
+                assert torch.equal(getattr(cos[0], name), getattr(cos[1], name)), name
+            assert torch.equal(hots[0], hots[1])
+    for p in pools:
+        p.destroy()
+
+
+def test_sieve_import_validation():
+    mod = kv()
+    with pytest.raises(RuntimeError, match="node_num"):
+        mod.sieve_import(*([1] * 11), 16, 16, 16, 64, 1, 1, [], 0, 1, 1152, 1, 1, 1, 0)
+    with pytest.raises(RuntimeError, match="padded_buffer_size"):
+        mod.sieve_import(*([1] * 11), 16, 16, 17, 64, 1, 1, [1], 0, 1, 1152, 1, 1, 1, 0)
+    with pytest.raises(RuntimeError, match="blockDim"):
+        mod.sieve_import(*([1] * 11), 16, 16, 16, 64, 1, 1, [1], 0, 1, 1152, 1, 1, 1, 0, 0, 9)
+    with pytest.raises(ValueError, match="path"):
+        mod.sieve_import(*([1] * 11), 16, 16, 16, 64, 1, 1, [1], 0, 1, 1152, 1, 1, 1, 0, path="fast")

@@ -17,7 +17,7 @@ RB = 1152
 
 class Opts(ctypes.Structure):
     _fields_ = [("hot_req_stride_rows", ctypes.c_uint64), ("injective", ctypes.c_uint32),
-                ("reserved", ctypes.c_uint32)]
+                ("step_path", ctypes.c_uint32)]
 
 
 def _lib():
