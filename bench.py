@@ -408,8 +408,8 @@ def report_b200(args, world, gathered, co):
                          peak_kind, None)
         else:
             traffic = None
-            if "gather_per_row" in tr and "sieve_per_request" in tr:
-                traffic = tr["gather_per_row"] * rows_per_launch + tr["sieve_per_request"] * R
+            if "coop_per_launch" in tr:  # measured at 33,477 rows per launch; scaled by rows
+                traffic = tr["coop_per_launch"] * rows_per_launch / 33477.0
             dominant = roof(name, "hbm", hbm_bytes, t, hbm_peak, peak_kind, traffic)
             other = None
     else:
