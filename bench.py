@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="layers per decode step (61 = config 2)")
     ap.add_argument("--path", choices=["auto", "coop", "fused", "split"], default="auto",
                     help="layer-step path of sieve_and_read (auto: cooperative when it fits)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the per-call loop only (default: `value` from decode steps replayed as CUDA graphs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -247,35 +249,61 @@ def run_b200(args):
     def layer_step(s, l):
         pool.sieve_and_read(co, l, topk[s, l], hot[l], stream, 1, hot_req_stride_rows=dbs, path=args.path)
 
-    for s in range(W):
-        for l in range(L):
-            layer_step(s, l)
+    def timed_pass(graphs):
+        """W untimed then S timed steps from the admitted state; device time of the S steps,
+        per-layer-step times, clock record. graphs: replay one captured graph per step, else
+        one call per layer with CUDA events around each call."""
+        co.admit_all(pre, base)
+        for s in range(W):
+            if graphs:
+                graphs[s].replay()
+            else:
+                for l in range(L):
+                    layer_step(s, l)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(S * (1 if graphs else L))]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks = ClockSampler(torch, local)
+        clocks.start()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.nvtx.range_push("timed" if graphs or args.no_graph else "per_call")  # profiler selection
+        t0.record()
+        for s in range(W, T):
+            if graphs:
+                e = evs[s - W]
+                e[0].record()
+                graphs[s].replay()
+                e[1].record()
+                continue
+            for l in range(L):
+                e = evs[(s - W) * L + l]
+                e[0].record()
+                layer_step(s, l)
+                e[1].record()
+        t1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        barrier()
+        clk = clocks.stop()
+        assert int(co.is_miss.sum().item()) == int(misses_h[T - 1, L - 1]), "replay diverged from the input pass"
+        return (t0.elapsed_time(t1) * 1e-3, [e[0].elapsed_time(e[1]) * 1e3 / (L if graphs else 1) for e in evs], clk)
+
+    # Per call: the public one-call API per layer, status words published (what a caller of
+    # sieve_and_read gets without graphs).
+    elapsed_pc, step_us_pc, clk_pc = timed_pass(None)
     path = mod.last_step_path()
     fused = path in ("coop", "fused")  # one kernel per layer-step
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(S * L)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(torch, local)
-    clocks.start()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.nvtx.range_push("timed")  # lets a profiler select exactly the timed launches
-    t0.record()
-    for s in range(W, T):
-        for l in range(L):
-            e = evs[(s - W) * L + l]
-            e[0].record()
-            layer_step(s, l)
-            e[1].record()
-    t1.record()
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
+    graphs = None
+    if not args.no_graph:  # one CUDA graph per decode step (its layers' calls), replayed in order
+        from kv_offload_proto_b200.graph import StepGraph
+        graphs = [StepGraph(pool, co, hot, L, path=args.path, hot_req_stride_rows=dbs, topk=topk[s]) for s in range(T)]
+        elapsed, step_us, clk = timed_pass(graphs)
+    else:
+        elapsed, step_us, clk = elapsed_pc, step_us_pc, clk_pc
     last = int(co.is_miss.sum().item())
-    assert last == int(misses_h[T - 1, L - 1]), "replay diverged from the input pass"
-    elapsed = t0.elapsed_time(t1) * 1e-3
-    step_us = [e[0].elapsed_time(e[1]) * 1e3 for e in evs]
     miss_rows = int(misses_h[W:].sum())
+    per_call = {"value": miss_rows * ROW_BYTES / elapsed_pc / 1e9, "unit": "GB/s",
+                "ms_per_step": elapsed_pc * 1e3 / S, "step_us": step_us_pc, "clocks": clk_pc}
 
     # Kernel durations for the roofline: the same steps replayed from the admitted state with
     # an event around each kernel (an event between the two kernels also stops the gather from
@@ -310,7 +338,8 @@ def run_b200(args):
                                                    args.path)
 
     res = dict(elapsed=elapsed, miss_rows=miss_rows, kernels=kernels, step_us=step_us, e2e=e2e, clocks=clk,
-               nodes=len(nodes), fused=fused, path=path)
+               nodes=len(nodes), fused=fused, path=path, graph=bool(graphs), per_call=per_call,
+               launches=len(kev))
     if world > 1:
         gathered = [None] * world
         dist.all_gather_object(gathered, res)
@@ -382,8 +411,7 @@ def report_b200(args, world, gathered, co):
     value = miss_rows * ROW_BYTES / elapsed / 1e9
     g0 = gathered[0]
     kern = {k: sum(v) / len(v) for k, v in g0["kernels"].items()}
-    n = len(g0["step_us"])
-    rows_per_launch = g0["miss_rows"] / n
+    rows_per_launch = g0["miss_rows"] / g0["launches"]
     remote = world > 1
     tr = traffic_per_unit()
     sb = state_bytes(co.padded_buffer_size, co.visited_stride_b, co.ht_size)
@@ -400,6 +428,8 @@ def report_b200(args, world, gathered, co):
 
     if g0["fused"]:
         (name, t), = kern.items()
+        if g0["graph"]:  # one kernel per layer-step: the timed region's device time per launch
+            t = max(g["elapsed"] for g in gathered) * 1e6 / (L * args.steps)
         hbm_bytes = s_bytes + hbm_gather
         if remote:  # rows cross NVLink; this GPU's HBM holds the state and the hot rows
             dominant = roof(name, "nvlink", rows_per_launch * ROW_BYTES, t, 770.0,
@@ -430,13 +460,26 @@ def report_b200(args, world, gathered, co):
                        world - 1),
                    "l2": "inputs larger than L2 (SIEVE state {:.0f} MB, pool {:.1f} GB per GPU)".format(
                        L * R * sb / 1e6, L * R * CFG["ctx"] * ROW_BYTES / 1e9),
-                   "step": "one decode step = {} layers x sieve_and_read, path {} ({})".format(
+                   "step": "one decode step = {} layers x sieve_and_read, path {} ({}){}".format(
                        L, g0["path"], {"coop": "one cooperative kernel: SIEVE CTAs + row-copy CTAs",
                                        "fused": "one kernel: SIEVE + bulk-copy warp",
-                                       "split": "SIEVE kernel + gather as programmatic dependent"}[g0["path"]])},
+                                       "split": "SIEVE kernel + gather as programmatic dependent"}[g0["path"]],
+                       ", each step replayed as one CUDA graph (no status words; completion on the stream)"
+                       if g0["graph"] else "")},
         "p50_us_per_layer_step": pct(steps_all, 50), "p99_us_per_layer_step": pct(steps_all, 99),
+        "graph": g0["graph"],
+        "per_layer_step_timing": "decode-step graph time / layers" if g0["graph"] else "CUDA events around each call",
+        "per_call": {"value": sum(g["miss_rows"] for g in gathered) * ROW_BYTES /
+                              max(g["per_call"]["ms_per_step"] for g in gathered) / args.steps / 1e6,
+                     "unit": "GB/s", "ms_per_step": max(g["per_call"]["ms_per_step"] for g in gathered),
+                     "p50_us_per_layer_step": pct([x for g in gathered for x in g["per_call"]["step_us"]], 50),
+                     "p99_us_per_layer_step": pct([x for g in gathered for x in g["per_call"]["step_us"]], 99),
+                     "note": "one sieve_and_read call per layer with status words, CUDA events around each call"},
         "kernel_avg_us": kern,
-        "kernel_timing": "separate replay of the same steps with CUDA events around each kernel",
+        "kernel_timing": "kernel_avg_us: separate replay of the same steps with CUDA events around each kernel "
+                         "(includes each launch's gap); roofline avg_us: " + (
+                             "timed-region device time / launches (one kernel per layer-step)"
+                             if g0["fused"] and g0["graph"] else "kernel_avg_us"),
         "miss_rows_per_layer_step": rows_per_launch,
         "roofline": dominant, "roofline_other": other,
         "gpu_launches": (1 if g0["fused"] else 2) * L * args.steps,

@@ -184,6 +184,12 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
  * kvops_sieve_import ran (KVOPS_STEP_AUTO before any). No counterpart in the reference. */
 uint32_t kvops_last_step_path(void);
 
+/* Does, without launching, the one-time setup the first kvops_sieve_import of this shape on
+ * the current device would do (device bookkeeping, cooperative-step scratch, kernel limits),
+ * so that later calls may be captured into a CUDA graph. No counterpart in the reference. */
+int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
+                       uint32_t visited_stride_b, uint32_t max_num_reqs);
+
 /* No counterpart in the reference. kvops_import_multi for callers that cannot allocate
  * device memory (an engine whose HBM is owned by its own allocator or fixed budget, or a
  * decode loop that cannot pay for cudaMalloc/cudaFree): it calls no allocating routine.

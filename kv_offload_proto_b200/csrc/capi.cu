@@ -336,22 +336,31 @@ bool vec16_ok(const kvb::GatherParams &g)
     return (a & 15) == 0;
 }
 
+// Allocates (once per device) the zeroed ready words of cooperative layer-steps.
+int ensure_ready_words(DeviceState *ds)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ds->ready != nullptr) return KVOPS_OK;
+    const size_t bytes = sizeof(uint32_t) * kReadyBlocks * kReadyWords;
+    cudaError_t e = cudaMalloc(&ds->ready, bytes);
+    if (e != cudaSuccess) {
+        ds->ready = nullptr;
+        return cuda_fail(e, "cudaMalloc(ready words)");
+    }
+    e = cudaMemset(ds->ready, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(ds->ready);
+        ds->ready = nullptr;
+        return cuda_fail(e, "cudaMemset(ready words)");
+    }
+    return KVOPS_OK;
+}
+
 // The ready words for the next cooperative layer-step on this device.
 int next_ready_block(DeviceState *ds, uint32_t **words)
 {
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if (ds->ready == nullptr) {
-            const size_t bytes = sizeof(uint32_t) * kReadyBlocks * kReadyWords;
-            cudaError_t e = cudaMalloc(&ds->ready, bytes);
-            if (e != cudaSuccess) {
-                ds->ready = nullptr;
-                return cuda_fail(e, "cudaMalloc(ready words)");
-            }
-            e = cudaMemset(ds->ready, 0, bytes);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(ready words)");
-        }
-    }
+    const int rc = ensure_ready_words(ds);
+    if (rc != KVOPS_OK) return rc;
     const uint32_t n = ds->ready_next.fetch_add(1, std::memory_order_relaxed);
     *words = ds->ready + static_cast<size_t>(n % kReadyBlocks) * kReadyWords;
     return KVOPS_OK;
@@ -650,6 +659,29 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
 }
 
 uint32_t kvops_last_step_path(void) { return t_last_step_path; }
+
+int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
+                       uint32_t visited_stride_b, uint32_t max_num_reqs)
+{
+    KV_REQUIRE_INIT();
+    DeviceState *ds = nullptr;
+    int rc = current_device_state(&ds);
+    if (rc != KVOPS_OK) return rc;
+    rc = ensure_ready_words(ds);
+    if (rc != KVOPS_OK) return rc;
+    int64_t ht_size = 1024;
+    while (ht_size < 2 * (static_cast<int64_t>(padded_buffer_size) + top_k)) ht_size <<= 1;
+    kvb::SieveParams p{};
+    p.top_k = static_cast<int32_t>(top_k);
+    p.dbs = static_cast<int32_t>(device_buffer_size);
+    p.padded = static_cast<int32_t>(padded_buffer_size);
+    p.vis_stride = static_cast<int32_t>(visited_stride_b);
+    p.max_num_reqs = static_cast<int32_t>(max_num_reqs);
+    p.ht_size = static_cast<int32_t>(ht_size);
+    cudaError_t e = kvb::prepare_sieve_coop(p);
+    if (e != cudaSuccess) return cuda_fail(e, "step_prepare");
+    return KVOPS_OK;
+}
 
 int kvops_sieve_ht_init(uint64_t device_buffer_tokens, uint64_t device_buffer_ht, uint64_t prefill_lens,
                         uint32_t req_start, uint32_t num_reqs, uint32_t layer_num, uint32_t pool_size,

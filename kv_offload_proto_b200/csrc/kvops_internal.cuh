@@ -160,5 +160,8 @@ cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cud
 // beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
 cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
                               bool *launched);
+// Sets up, without launching, what the first cooperative step of this shape would: the
+// kernel's shared-memory limit and the cached residency (so a later call may be captured).
+cudaError_t prepare_sieve_coop(const SieveParams &p);
 
 }  // namespace kvb

@@ -200,6 +200,10 @@ PYBIND11_MODULE(_kvops, m)
           py::arg("hot_row_base"), py::arg("stripe_rows"), py::arg("status"), py::arg("stream") = 0,
           py::arg("block_dim") = 1, py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false,
           py::arg("path") = "auto");
+    m.def("step_prepare", [](uint32_t top_k, uint32_t dbs, uint32_t padded, uint32_t vis_stride, uint32_t max_num_reqs) {
+        check(kvops_step_prepare(top_k, dbs, padded, vis_stride, max_num_reqs));
+    }, py::arg("top_k"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"), py::arg("visited_stride_b"),
+          py::arg("max_num_reqs"));
     m.def("last_step_path", []() {
         switch (kvops_last_step_path()) {
             case KVOPS_STEP_COOP: return std::string("coop");

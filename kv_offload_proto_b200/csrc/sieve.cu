@@ -1526,15 +1526,28 @@ cudaError_t coop_residency(size_t smem, int *resident)
     return cudaSuccess;
 }
 
+// Dynamic shared memory of a cooperative step: the SIEVE layout, or the copy CTAs' two row lists.
+size_t coop_smem(const SieveParams &p)
+{
+    const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
+    const size_t list = 4ull * sizeof(void *) * kFastThreads;
+    return F.total > list ? F.total : list;
+}
+
+cudaError_t prepare_sieve_coop(const SieveParams &p)
+{
+    if (p.top_k <= 0 || p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return cudaSuccess;
+    int resident = 0;
+    return coop_residency(coop_smem(p), &resident);
+}
+
 cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
                               bool *launched)
 {
     *launched = false;
     if (p.max_num_reqs <= 0 || p.top_k <= 0 || p.max_num_reqs > kMaxCoopReqs) return cudaSuccess;
     if (p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return cudaSuccess;
-    const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
-    const size_t list = 4ull * sizeof(void *) * kFastThreads;  // two row lists of copy_ready_rows
-    const size_t total = F.total > list ? F.total : list;
+    const size_t total = coop_smem(p);
     int resident = 0;
     cudaError_t e = coop_residency(total, &resident);
     if (e != cudaSuccess) return e;
