@@ -601,36 +601,39 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
     return true;
 }
 
-// 2c: final visited bits of the slots passed, one word per thread.
+// 2c: final visited bits of the slots passed: one slot per lane, one 32-slot word per warp
+// (the word's bits are gathered by ballot).
 __device__ void passed_bits(const uint32_t *vini, uint32_t *vfin, const uint32_t *tf, const uint16_t *evt,
                             const uint32_t *cand, const uint32_t *wofs, int32_t n, int32_t dbs, int32_t hand0,
                             int32_t last)
 {
+    const unsigned kAll = 0xFFFFFFFFu;
     const int32_t nwords = (dbs + 31) >> 5;
     const int32_t pend = (last - hand0 + dbs) % dbs + 1;  // slots passed, in sweep order from the hand
-    for (int32_t w = threadIdx.x; w < nwords; w += blockDim.x) {
-        uint32_t m = 0u, b = 0u;
-        int32_t q = static_cast<int32_t>(wofs[w]);  // candidates before this slot, slot order
+    const int lane = threadIdx.x & 31;
+    const int32_t nwarps = static_cast<int32_t>(blockDim.x >> 5);
+    for (int32_t w = static_cast<int32_t>(threadIdx.x >> 5); w < nwords; w += nwarps) {
+        const int32_t c = (w << 5) + lane;
         const uint32_t ini = vini[w];
-        for (int l = 0; l < 32; ++l) {
-            const int32_t c = (w << 5) + l;
-            if (c >= dbs) break;
-            const bool is_cand = ((ini >> l) & 1u) == 0u;
+        bool in = false, bit = false;
+        if (c < dbs) {
             int32_t pos = c - hand0;
             if (pos < 0) pos += dbs;
             if (pos < pend) {
-                m |= 1u << l;
+                in = true;
                 if (evt[c] != kNone16) {
-                    b |= 1u << l;
+                    bit = true;
                 } else {
-                    const uint32_t arr = cand[q == n ? 0 : q] >> 16;  // next candidate at or after c
+                    // candidates before c in slot order; the one at that index is the next at or after c
+                    const int32_t q = static_cast<int32_t>(wofs[w]) + __popc(~ini & ((1u << lane) - 1u));
+                    const uint32_t arr = cand[q == n ? 0 : q] >> 16;
                     const uint32_t x = tf[c];
-                    if ((x & 0xFFFFu) != kNone16 && (x >> 16) > arr) b |= 1u << l;
+                    bit = (x & 0xFFFFu) != kNone16 && (x >> 16) > arr;
                 }
             }
-            if (is_cand) ++q;
         }
-        if (m) vfin[w] = (vfin[w] & ~m) | (b & m);
+        const uint32_t m = __ballot_sync(kAll, in), bits = __ballot_sync(kAll, bit);
+        if (lane == 0 && m) vfin[w] = (vfin[w] & ~m) | (bits & m);
     }
 }
 
