@@ -355,7 +355,7 @@ constexpr uint16_t kLeadMark = 0xFFFEu;  // table cell: first deleted entry of i
 constexpr uint8_t kClsNone = 0, kClsRes = 1, kClsNew = 2, kClsPending = 3, kClsPlaced = 4;
 
 struct FastLayout {
-    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, missb, wofs, total;
+    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, posl, missb, wofs, total;
     int32_t dcap;
 };
 
@@ -384,10 +384,12 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
     L.evt = take(&o, 2ull * padded);
     L.vini = take(&o, static_cast<size_t>(vis_stride));
     L.vfin = take(&o, static_cast<size_t>(vis_stride));
-    // The dedup table (phase 1) and the candidate list (phase 2) share one region.
-    const size_t dd = 8ull * L.dcap > 4ull * dbs + 16 ? 8ull * L.dcap : 4ull * dbs + 16;  // +16: whole 16-B chunks
+    // The dedup table (phase 1) and the candidate list + miss positions (phase 2) share one region.
+    const size_t cl = align_up(4ull * dbs + 16, 16);  // +16: whole 16-B chunks
+    const size_t dd = 8ull * L.dcap > cl + 2ull * K ? 8ull * L.dcap : cl + 2ull * K;
     L.dkey = take(&o, dd);
     L.dfirst = L.dkey + 4ull * L.dcap;
+    L.posl = L.dkey + cl;
     L.missb = take(&o, 4ull * ((K + 31) / 32));
     L.wofs = take(&o, 4ull * ((dbs + 31) / 32 + 1));
     L.total = o;
@@ -471,48 +473,47 @@ __device__ __forceinline__ int select_bit(uint32_t v, int32_t n)
 }
 
 // 2b: the walk (one warp), 32 candidates per batch, one per lane, in sweep order from the
-// hand. One round resolves many candidates at once:
-//  - the window: the next (up to) 32 queued misses at or after tq (32 queue words);
-//  - each lane ranks its token's first lookup Tf among them: t_j = misses in the window
-//    before Tf (a lookup before tq ranks 0; none, or one past the window, ranks all);
-//  - the sweep with this queue is the recurrence k <- k + (k < t_j) over the lanes: the
-//    lane is reached by the window's miss number k and evicted iff k < t_j;
+// hand. Misses are consumed in position order, so the m-th consumed miss is the m-th set bit
+// of the final miss queue: the walk records miss numbers, and a parallel pass afterwards turns
+// them into positions. One round resolves many candidates at once:
+//  - the window: the queue words w0 .. w0+31, of which the first s0 misses are consumed
+//    (created misses always land after the consumed ones, so s0 stays exact);
+//  - each lane ranks its token's first lookup Tf among the window's unconsumed misses: t_j =
+//    those before Tf (a lookup before them ranks 0; none, or one past the window, ranks all);
+//  - the sweep with this queue is the recurrence k <- k + (k < t_j) over the lanes: the lane
+//    is reached by unconsumed miss number k and evicted iff k < t_j; only lanes with
+//    0 < t_j < 32 need k first;
 //  - an evicted lane whose token is looked up later creates the miss Tf, which this queue
 //    lacks. Every lane reached before the earliest such Tf (cmin) is exact, since the queue
-//    is exact below cmin; those lanes, always at least the first one, are committed and the
-//    created misses join the shared queue. The next round starts after the last eviction.
-// Each round commits a lane or moves the window past 1024 empty positions, which bounds the
-// rounds. Returns false when the sweep would pass a slot twice (misses remain after every
-// candidate), or if the bound were ever exceeded.
-__device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t *evt, uint32_t *missb,
-                                int32_t *os, int8_t *om, int32_t K, int32_t *last_out)
+//    is exact below cmin; those lanes, always at least the first one, are committed with
+//    arrival number G + k (G: misses consumed before the round), evicted slots get evt = that
+//    number, and the created misses join the queue.
+// Each round commits a lane, or moves the window: past 32 fully consumed words, or up to the
+// word of the next unconsumed miss (at most once per commit), which bounds the rounds.
+// Returns false when the sweep would pass a slot twice (misses remain after every candidate),
+// or if the bound were ever exceeded. *nvis_out: candidates visited (a prefix of sweep order).
+__device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t *evt, uint32_t *missb, int32_t K,
+                                int32_t *last_out, int32_t *nvis_out)
 {
     const unsigned kAll = 0xFFFFFFFFu;
     const int lane = threadIdx.x & 31;
     const int32_t qwords = (K + 31) >> 5;
-    int32_t tq = 0;  // first position the sweep has not consumed
-    int32_t last = -1;
+    int32_t w0 = 0, s0 = 0, G = 0, last = -1, nvis = 0;
     bool done = false;
-    int32_t rounds = n + (qwords >> 5) + 2;
+    int32_t rounds = 2 * n + (qwords >> 5) + 4;
     // sweep position s (0 <= s < n) is candidate index (n0 + s) mod n
-    auto index_of = [&](int32_t s) { return n0 + s >= n ? n0 + s - n : n0 + s; };
+    auto index_of = [&](int32_t sp) { return n0 + sp >= n ? n0 + sp - n : n0 + sp; };
     uint32_t xnext = lane < n ? cand[index_of(lane)] : 0u;
-    for (int32_t s0 = 0; s0 < n && !done; s0 += 32) {
+    for (int32_t sb = 0; sb < n && !done; sb += 32) {
         const uint32_t xv = xnext;
         const uint32_t f = xv >> 16;
-        const int32_t cnt = min(32, n - s0);
-        const int32_t my = index_of(s0 + lane < n ? s0 + lane : 0);
-        if (s0 + 32 + lane < n) xnext = cand[index_of(s0 + 32 + lane)];  // next batch, loaded ahead
+        const int32_t cnt = min(32, n - sb);
+        const int32_t my = index_of(sb + lane < n ? sb + lane : 0);
+        if (sb + 32 + lane < n) xnext = cand[index_of(sb + 32 + lane)];  // next batch, loaded ahead
         int cur = 0;
         while (cur < cnt) {
             if (--rounds < 0) return false;
-            const int32_t w0 = tq >> 5;
-            const uint32_t low = 0xFFFFFFFFu << (tq & 31);  // word w0: positions >= tq
-            uint32_t W = w0 + lane < qwords ? missb[w0 + lane] : 0u;
-            if (lane == 0) W &= low;
-            const int32_t wf = f == kNone16 ? 32 : static_cast<int32_t>(f >> 5) - w0;  // lookup's word
-            uint32_t ws = wf >= 0 && wf < 32 && w0 + wf < qwords ? missb[w0 + wf] : 0u;
-            if (wf == 0) ws &= low;
+            const uint32_t W = w0 + lane < qwords ? missb[w0 + lane] : 0u;
             const uint32_t pop = static_cast<uint32_t>(__popc(W));
             // the words' miss counts, bit-sliced over six ballots (counts are 0..32)
             uint32_t bs[6];
@@ -524,21 +525,39 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
                 for (int b = 0; b < 6; ++b) c += __popc(bs[b] & lanes) << b;
                 return c;
             };
-            const int32_t mtot = before(kAll);
-            if (mtot == 0) {  // no queued miss in these 32 words
+            const int32_t avail = before(kAll) - s0;
+            if (avail <= 0) {  // every miss in these 32 words is consumed
                 if (w0 + 32 >= qwords) {
                     done = true;
                     break;
                 }
-                tq = (w0 + 32) << 5;
+                w0 += 32;
+                s0 = 0;
                 continue;
             }
-            const int32_t mw = min(32, mtot);
+            if (avail < 32 && w0 + 32 < qwords) {  // move up to the word of the next unconsumed miss
+                const int32_t e_me = before((1u << lane) - 1u);
+                const int ls = __ffs(__ballot_sync(kAll, e_me + static_cast<int32_t>(pop) > s0)) - 1;
+                if (ls > 0) {
+                    s0 -= __shfl_sync(kAll, e_me, ls);
+                    w0 += ls;
+                    continue;
+                }
+            }
+            const int32_t mw = min(32, avail);
             const bool live = lane >= cur && lane < cnt;
+            const int32_t wf = f == kNone16 ? 32 : static_cast<int32_t>(f >> 5) - w0;
+            const int src = wf < 0 ? 0 : (wf > 31 ? 31 : wf);
+            const uint32_t ws = __shfl_sync(kAll, W, src);
             int32_t tj = 0;
-            if (live)
-                tj = wf >= 32 ? mw
-                              : (wf < 0 ? 0 : min(mw, before((1u << wf) - 1u) + __popc(ws & ((1u << (f & 31)) - 1u))));
+            if (live) {
+                if (wf >= 32) {
+                    tj = mw;
+                } else if (wf >= 0) {
+                    const int32_t r = before((1u << src) - 1u) + __popc(ws & ((1u << (f & 31)) - 1u)) - s0;
+                    tj = r < 0 ? 0 : (r > mw ? mw : r);
+                }
+            }
             // t_j = 0 always passes and t_j = mw always evicts once reached; only a lane whose
             // lookup falls inside the window needs its k_j first, taken in lane order.
             uint32_t evm = __ballot_sync(kAll, live && tj >= mw);
@@ -552,53 +571,95 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
             const int32_t myk = __popc(evm & ((1u << lane) - 1u));
             const bool reached = live && myk < mw;
             const bool ev = reached && ((evm >> lane) & 1u);
-            // arrival: the window's miss number myk. Its word is the last non-empty word whose
-            // first miss number is <= myk: marks (bit = first miss number of each non-empty
-            // word) count them, and the non-empty words' ballot gives its lane.
-            const int32_t e_me = before((1u << lane) - 1u);
-            const uint32_t nonempty = __ballot_sync(kAll, pop != 0u);
-            const uint32_t marks = __reduce_or_sync(kAll, pop != 0u && e_me < 32 ? 1u << e_me : 0u);
-            const int32_t r = min(myk, 31);
-            const int lo = select_bit(nonempty, __popc(marks & (0xFFFFFFFFu >> (31 - r))) - 1);
-            uint32_t x = w0 + lo < qwords ? missb[w0 + lo] : 0u;
-            if (lo == 0) x &= low;
-            const int pos = select_bit(x, r - before((1u << lo) - 1u));
-            const uint32_t arr = reached ? static_cast<uint32_t>(((w0 + lo) << 5) + pos) : 0xFFFFFFFFu;
+            // the earliest miss this round creates, ranked among the window's unconsumed misses
             const uint32_t cmin = __reduce_min_sync(kAll, ev && f != kNone16 ? f : 0xFFFFFFFFu);
-            const bool com = reached && arr < cmin;
+            int32_t rc = 0x7FFFFFFF;
+            if (cmin != 0xFFFFFFFFu) {
+                const int32_t wc = static_cast<int32_t>(cmin >> 5) - w0;  // >= 0: cmin follows a reached miss
+                const uint32_t wcs = __shfl_sync(kAll, W, wc < 32 ? wc : 0);
+                if (wc < 32) rc = before((1u << wc) - 1u) + __popc(wcs & ((1u << (cmin & 31)) - 1u)) - s0;
+            }
+            const bool com = reached && myk < rc;
             const uint32_t cm = __ballot_sync(kAll, com);
-            const uint32_t slot = xv & 0xFFFFu;
+            const uint32_t em = __ballot_sync(kAll, com && ev);
             if (com) {
-                cand[my] = (arr << 16) | slot;
+                const uint32_t slot = xv & 0xFFFFu;
+                const uint32_t num = static_cast<uint32_t>(G + myk);
+                cand[my] = (num << 16) | slot;
                 if (ev) {
-                    os[arr] = static_cast<int32_t>(slot);
-                    om[arr] = 1;
-                    evt[slot] = static_cast<uint16_t>(arr);
+                    evt[slot] = static_cast<uint16_t>(num);
                     if (f != kNone16) atomicOr(&missb[f >> 5], 1u << (f & 31));  // created miss
                 }
             }
-            // the last eviction committed (arrival times rise along the lanes): +1 so 0 = none
-            const uint32_t le = __reduce_max_sync(kAll, com && ev ? ((arr << 16) | slot) + 1u : 0u);
-            if (le) {
-                last = static_cast<int32_t>((le - 1u) & 0xFFFFu);
-                tq = static_cast<int32_t>((le - 1u) >> 16) + 1;
-            }
+            if (em) last = static_cast<int32_t>(__shfl_sync(kAll, xv, 31 - __clz(em)) & 0xFFFFu);
+            const int32_t ec = __popc(em);
+            G += ec;
+            s0 += ec;
             if (cm == 0u) return false;  // cannot happen: the first lane is always committed
             cur = 32 - __clz(cm);
+            nvis = sb + cur;
             __syncwarp();  // created misses visible before the next round reads the queue
         }
     }
-    if (!done) {  // every candidate was visited: misses left over mean the sweep would wrap
-        bool rem = false;
-        for (int32_t w = (tq >> 5) + lane; w < qwords; w += 32) {
-            uint32_t W = missb[w];
-            if (w == (tq >> 5)) W &= 0xFFFFFFFFu << (tq & 31);
-            rem |= W != 0u;
-        }
-        if (__any_sync(kAll, rem)) return false;
+    if (!done) {  // every candidate was visited: unconsumed misses mean the sweep would wrap
+        int32_t rem = 0;
+        for (int32_t w = w0 + lane; w < qwords; w += 32) rem += __popc(missb[w]);
+        for (int d = 16; d >= 1; d >>= 1) rem += __shfl_xor_sync(kAll, rem, d);
+        if (rem - s0 > 0) return false;
     }
     *last_out = last;
+    *nvis_out = nvis;
     return true;
+}
+
+// 2b': miss numbers -> positions. posl[m] = position of the m-th set bit of the miss queue
+// (all threads), then every evicted slot's number and every visited candidate's arrival
+// number is replaced by its position, and the misses' outputs are written.
+__device__ void resolve_miss_numbers(const uint32_t *missb, int32_t K, uint16_t *posl, uint16_t *evt, int32_t *os,
+                                     int8_t *om, uint32_t *cand, int32_t n, int32_t n0, int32_t nvis, int32_t dbs,
+                                     int32_t *warp_sums)
+{
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+    const int32_t nwords = (K + 31) >> 5;
+    const int32_t per = (nwords + nt - 1) / nt;
+    const int32_t w0 = min(tid * per, nwords), w1 = min(w0 + per, nwords);
+    int32_t mine = 0;
+    for (int32_t w = w0; w < w1; ++w) mine += __popc(missb[w]);
+    int32_t incl = mine;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = nt >> 5;
+        int32_t v = lane < nw ? warp_sums[lane] : 0, inc = v;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int32_t u = __shfl_up_sync(0xFFFFFFFFu, inc, d);
+            if (lane >= d) inc += u;
+        }
+        if (lane < nw) warp_sums[lane] = inc - v;
+    }
+    __syncthreads();
+    int32_t at = warp_sums[wid] + incl - mine;
+    for (int32_t w = w0; w < w1; ++w) {
+        for (uint32_t b = missb[w]; b; b &= b - 1u) posl[at++] = static_cast<uint16_t>((w << 5) + __ffs(b) - 1);
+    }
+    __syncthreads();
+    for (int32_t c = tid; c < dbs; c += nt) {
+        const uint16_t m = evt[c];
+        if (m == kNone16) continue;
+        const uint16_t pos = posl[m];
+        evt[c] = pos;
+        os[pos] = c;
+        om[pos] = 1;
+    }
+    for (int32_t sp = tid; sp < nvis; sp += nt) {
+        const int32_t i = n0 + sp >= n ? n0 + sp - n : n0 + sp;
+        const uint32_t x = cand[i];
+        cand[i] = (static_cast<uint32_t>(posl[x >> 16]) << 16) | (x & 0xFFFFu);
+    }
 }
 
 // 2c: final visited bits of the slots passed: one slot per lane, one 32-slot word per warp
@@ -1017,7 +1078,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __shared__ int32_t s_hand;
     __shared__ bool s_dirty;
     __shared__ int32_t s_warp[32];
-    __shared__ int32_t s_ncand, s_last, s_nkeys;
+    __shared__ int32_t s_ncand, s_last, s_nkeys, s_n0, s_nvis;
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -1165,12 +1226,14 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         int32_t n0 = static_cast<int32_t>(s_wofs[h0 >> 5]) +
                      __popc(~s_vini[h0 >> 5] & ((1u << (h0 & 31)) - 1u));
         if (n0 >= n) n0 = 0;
-        int32_t last = -1;
-        const bool ok = walk_candidates(s_cand, n, n0, s_evt, s_missb, s_os, s_om, K, &last);
+        int32_t last = -1, nvis = 0;
+        const bool ok = walk_candidates(s_cand, n, n0, s_evt, s_missb, K, &last, &nvis);
         if (tid == 0) {
             if (!ok) s_flag = 1;
             s_last = last;
             s_any_miss = last >= 0;
+            s_n0 = n0;
+            s_nvis = nvis;
         }
     } else if (kMode == 2 && !s_flag) {
         // Cooperative step: while one warp walks, the others start pulling this request's
@@ -1187,6 +1250,10 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             prefetch_l2(seg + (g.layer_offset_rows + seg_row) * static_cast<uint64_t>(g.row_bytes), g.row_bytes);
         }
     }
+    __syncthreads();
+    if (!s_flag)
+        resolve_miss_numbers(s_missb, K, reinterpret_cast<uint16_t *>(smem + L.posl), s_evt, s_os, s_om, s_cand,
+                             s_ncand, s_n0, s_nvis, dbs, s_warp);
     __syncthreads();
     if (!s_flag && s_last >= 0) {
         passed_bits(s_vini, s_vfin, s_tf, s_evt, s_cand, s_wofs, s_ncand, dbs, s_hand, s_last);
