@@ -126,6 +126,19 @@ int kvops_import_multi(uint32_t node_num, const uint64_t *seg_bases, uint32_t la
                        uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
                        uint32_t block_dim, const KvopsRowOpts *opts);
 
+/* The single-layer indexed export of decode increments, kvc_scatter_rows: designed in the
+ * reference with the arguments of kvc_gather_rows and the opposite data direction
+ * (doc/kv_offload_design.md:394-396), its implementation later deleted (:544). For every position
+ * (batch row < num_real, k < top_k) whose export_flags byte is set, with a valid token, slot and
+ * pool row on node my_node, copies the hot row (hot_row_base + slot, or the per-request stride
+ * of opts) to segment row segRow of layer_offset_rows -- kvops_import_seg's rules, reversed.
+ * Same status words and errCodes. Positions that name the same segment row race. */
+int kvops_export_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
+                     uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
+                     uint64_t topk_device_slots, uint64_t export_flags, uint64_t num_real, uint64_t hot_row_base,
+                     uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
+                     uint64_t status, uint64_t stream, uint32_t block_dim, const KvopsRowOpts *opts);
+
 /* Replaces kv_export_seg_alllayer + kvc_scatter_rows_alllayer (kvops_ext.cpp:256-278,
  * kvops/kernel/kvc_scatter_rows_alllayer.cpp:11-67): for every layer l and row in
  * [row_lo, row_lo+row_cnt) owned by my_node, the segment row

@@ -145,22 +145,24 @@ int build_gather(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo,
                   uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
                   uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base,
                   uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
-                  uint32_t block_dim, const KvopsRowOpts *opts, kvb::GatherParams *out, DeviceState **ds_out)
+                  uint32_t block_dim, const KvopsRowOpts *opts, kvb::GatherParams *out, DeviceState **ds_out,
+                  const char *what = "import")
 {
+    const std::string w(what);
     KV_REQUIRE_INIT();
-    if (block_dim > 8) return fail(KVOPS_E_INVALID, "import blockDim must be <= 8 (status slot layout)");
-    if (block_dim == 0) return fail(KVOPS_E_INVALID, "import blockDim must be >= 1");
+    if (block_dim > 8) return fail(KVOPS_E_INVALID, w + " blockDim must be <= 8 (status slot layout)");
+    if (block_dim == 0) return fail(KVOPS_E_INVALID, w + " blockDim must be >= 1");
     if (node_num == 0 || node_num > KVOPS_MAX_NODES)
-        return fail(KVOPS_E_INVALID, "import node_num must be in [1, 64]");
+        return fail(KVOPS_E_INVALID, w + " node_num must be in [1, 64]");
     if (my_node != kvb::kAllNodes && my_node >= node_num)
-        return fail(KVOPS_E_INVALID, "import my_node must be < node_num");
-    if (row_bytes == 0) return fail(KVOPS_E_INVALID, "import row_bytes must be > 0");
+        return fail(KVOPS_E_INVALID, w + " my_node must be < node_num");
+    if (row_bytes == 0) return fail(KVOPS_E_INVALID, w + " row_bytes must be > 0");
     if (max_num_reqs > 0 && top_k > 0 &&
         (topk_indices == 0 || req_pool_indices == 0 || req_host_base == 0 || topk_device_slots == 0 ||
          is_miss == 0 || num_real == 0 || hot_row_base == 0))
-        return fail(KVOPS_E_INVALID, "import: a tensor address is 0");
+        return fail(KVOPS_E_INVALID, w + ": a tensor address is 0");
     const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{0, 0, 0};
-    if (o.injective > 1) return fail(KVOPS_E_INVALID, "import: injective must be 0 or 1");
+    if (o.injective > 1) return fail(KVOPS_E_INVALID, w + ": injective must be 0 or 1");
     DeviceState *ds = nullptr;
     int rc = current_device_state(&ds);
     if (rc != KVOPS_OK) return rc;
@@ -526,6 +528,31 @@ int kvops_import_seg_ex(uint64_t channel, uint64_t seg_base, uint32_t layer_offs
     return import_common(node_num, segs, my_node, my_node + 1, my_node, layer_offset_rows, per_layer_seg_rows,
                          row_bytes, topk_indices, req_pool_indices, req_host_base, topk_device_slots, is_miss,
                          num_real, hot_row_base, top_k, max_num_reqs, stripe_rows, status, stream, block_dim, opts);
+}
+
+int kvops_export_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
+                     uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
+                     uint64_t topk_device_slots, uint64_t export_flags, uint64_t num_real, uint64_t hot_row_base,
+                     uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
+                     uint64_t status, uint64_t stream, uint32_t block_dim, const KvopsRowOpts *opts)
+{
+    (void)channel;
+    KV_REQUIRE_INIT();
+    if (node_num == 0 || node_num > KVOPS_MAX_NODES)
+        return fail(KVOPS_E_INVALID, "export_seg node_num must be in [1, 64]");
+    if (my_node >= node_num) return fail(KVOPS_E_INVALID, "export_seg my_node must be < node_num");
+    uint64_t segs[KVOPS_MAX_NODES] = {0};
+    segs[my_node] = seg_base;
+    kvb::GatherParams p{};
+    DeviceState *ds = nullptr;
+    int rc = build_gather(node_num, segs, my_node, my_node + 1, my_node, layer_offset_rows, per_layer_seg_rows,
+                          row_bytes, topk_indices, req_pool_indices, req_host_base, topk_device_slots, export_flags,
+                          num_real, hot_row_base, top_k, max_num_reqs, stripe_rows, status, stream, block_dim, opts,
+                          &p, &ds, "export_seg");
+    if (rc != KVOPS_OK) return rc;
+    cudaError_t e = kvb::launch_scatter(p, reinterpret_cast<cudaStream_t>(stream), ds->sm_count);
+    if (e != cudaSuccess) return cuda_fail(e, "launch kvc_scatter_rows");
+    return KVOPS_OK;
 }
 
 int kvops_import_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,

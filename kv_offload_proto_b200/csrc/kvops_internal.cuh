@@ -148,6 +148,9 @@ int set_last_error(int code, const char *msg);
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int sm_count);
 cudaError_t launch_sieve_ht_init(const HtInitParams &p, cudaStream_t s);
 cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count);
+// The gather's rules in the opposite direction (kvc_scatter_rows): hot row -> segment row for
+// every position whose flag (p.is_miss) is set.
+cudaError_t launch_scatter(const GatherParams &p, cudaStream_t s, int sm_count);
 cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count);
 // Fused SIEVE step + miss-row gather (one CTA per request). Sets *launched = false, launching
 // nothing, when the request's state and the copy ring do not fit shared memory; the caller

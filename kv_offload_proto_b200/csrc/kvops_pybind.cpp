@@ -102,6 +102,18 @@ void sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq
                              block_dim, &o));
 }
 
+void export_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows, uint32_t per_layer_seg_rows,
+                uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
+                uint64_t topk_device_slots, uint64_t export_flags, uint64_t num_real, uint64_t hot_row_base,
+                uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
+                uint64_t status, uint64_t stream, uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective)
+{
+    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    check(kvops_export_seg(channel, seg_base, layer_offset_rows, per_layer_seg_rows, row_bytes, topk_indices,
+                           req_pool_indices, req_host_base, topk_device_slots, export_flags, num_real, hot_row_base,
+                           top_k, max_num_reqs, stripe_rows, node_num, my_node, status, stream, block_dim, &o));
+}
+
 void export_seg_alllayer(uint64_t channel, uint64_t seg_base, uint32_t per_layer_seg_rows, uint32_t row_bytes,
                          uint32_t row_lo, uint32_t row_cnt, uint32_t layer_num, uint64_t src_layer0_base,
                          uint64_t src_layer_stride, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
@@ -179,6 +191,13 @@ PYBIND11_MODULE(_kvops, m)
           py::arg("hot_row_base"), py::arg("top_k"), py::arg("max_num_reqs"), py::arg("stripe_rows"),
           py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1, py::kw_only(),
           py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false);
+    // Single-layer indexed export (kvc_scatter_rows; designed in the reference, not in its module).
+    m.def("export_seg", &export_seg, py::arg("channel"), py::arg("seg_base"), py::arg("layer_offset_rows"),
+          py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("topk_indices"), py::arg("req_pool_indices"),
+          py::arg("req_host_base"), py::arg("topk_device_slots"), py::arg("export_flags"), py::arg("num_real"),
+          py::arg("hot_row_base"), py::arg("top_k"), py::arg("max_num_reqs"), py::arg("stripe_rows"),
+          py::arg("node_num"), py::arg("my_node"), py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1,
+          py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false);
     m.def("export_seg_alllayer", &export_seg_alllayer, py::arg("channel"), py::arg("seg_base"),
           py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("row_lo"), py::arg("row_cnt"),
           py::arg("layer_num"), py::arg("src_layer0_base"), py::arg("src_layer_stride"), py::arg("stripe_rows"),

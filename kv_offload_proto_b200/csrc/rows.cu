@@ -24,7 +24,7 @@ constexpr int kUnroll = 8;
 // tiles, so no wave is left partly empty.
 constexpr int kGatherTile = kRowThreads;
 
-template <typename V>
+template <typename V, bool kScatter>
 __global__ void __launch_bounds__(kRowThreads, 4) gather_kernel(const GatherParams p, uint32_t magic)
 {
     __shared__ const uint8_t *s_src[kGatherTile];
@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(kRowThreads, 4) gather_kernel(const GatherPara
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * kGatherTile; base < total;
          base += static_cast<int64_t>(gridDim.x) * kGatherTile) {
         const int64_t end = base + kGatherTile < total ? base + kGatherTile : total;
-        gather_tile<V, kUnroll, false>(p, base, end, s_src, s_dst, &s_n, magic);
+        gather_tile<V, kUnroll, false, kScatter>(p, base, end, s_src, s_dst, &s_n, magic);
     }
     __syncthreads();
     if (threadIdx.x == 0) arrive_and_publish(p.st);
@@ -137,7 +137,8 @@ int vec_bytes(uint64_t addr_or, uint32_t row_bytes)
 
 }  // namespace
 
-cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count)
+template <bool kScatter>
+cudaError_t launch_rows(const GatherParams &p, cudaStream_t s, int sm_count)
 {
     uint64_t addr_or = reinterpret_cast<uint64_t>(p.hot) | p.hot_req_stride_bytes;
     for (uint32_t n = 0; n < p.nodes && n < static_cast<uint32_t>(kMaxNodes); ++n)
@@ -164,11 +165,21 @@ cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count)
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     switch (vb) {
-        case 16: return cudaLaunchKernelEx(&cfg, gather_kernel<uint4>, p, magic);
-        case 8: return cudaLaunchKernelEx(&cfg, gather_kernel<uint2>, p, magic);
-        case 4: return cudaLaunchKernelEx(&cfg, gather_kernel<uint32_t>, p, magic);
-        default: return cudaLaunchKernelEx(&cfg, gather_kernel<uint8_t>, p, magic);
+        case 16: return cudaLaunchKernelEx(&cfg, gather_kernel<uint4, kScatter>, p, magic);
+        case 8: return cudaLaunchKernelEx(&cfg, gather_kernel<uint2, kScatter>, p, magic);
+        case 4: return cudaLaunchKernelEx(&cfg, gather_kernel<uint32_t, kScatter>, p, magic);
+        default: return cudaLaunchKernelEx(&cfg, gather_kernel<uint8_t, kScatter>, p, magic);
     }
+}
+
+cudaError_t launch_gather(const GatherParams &p, cudaStream_t s, int sm_count)
+{
+    return launch_rows<false>(p, s, sm_count);
+}
+
+cudaError_t launch_scatter(const GatherParams &p, cudaStream_t s, int sm_count)
+{
+    return launch_rows<true>(p, s, sm_count);
 }
 
 cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count)

@@ -106,8 +106,10 @@ __device__ __forceinline__ void list_append(bool ok, const uint8_t *src, uint8_t
 
 // Positions [base, end) of one tile (end - base <= blockDim.x): each thread evaluates one, the
 // accepted rows are appended to the shared list (warp-aggregated), and the CTA copies them.
-// s_n must be zero on entry and is zero again on return; ends with a barrier.
-template <typename V, int kUnroll, bool kFresh>
+// kScatter: the opposite direction (kvc_scatter_rows: hot row -> segment row) under the same
+// rules, with p.is_miss holding the export flags. s_n must be zero on entry and is zero again
+// on return; ends with a barrier.
+template <typename V, int kUnroll, bool kFresh, bool kScatter = false>
 __device__ __forceinline__ void gather_tile(const GatherParams &p, int64_t base, int64_t end, const uint8_t **s_src,
                                             uint8_t **s_dst, int *s_n, uint32_t magic)
 {
@@ -115,6 +117,11 @@ __device__ __forceinline__ void gather_tile(const GatherParams &p, int64_t base,
     const uint8_t *src = nullptr;
     uint8_t *dst = nullptr;
     const bool ok = pos < end && gather_position<kFresh>(p, pos, &src, &dst);
+    if (kScatter) {
+        const uint8_t *hot_row = dst;
+        dst = const_cast<uint8_t *>(src);
+        src = hot_row;
+    }
     list_append(ok, src, dst, s_src, s_dst, s_n);
     __syncthreads();
     cta_copy_rows<V, kUnroll>(s_src, s_dst, *s_n, p.row_bytes, magic);

@@ -455,23 +455,6 @@ __device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint3
     }
 }
 
-// Position of the n-th (from 0) set bit of v, by halving; n < popc(v) gives a set bit, any
-// other n some position in [0, 31].
-__device__ __forceinline__ int select_bit(uint32_t v, int32_t n)
-{
-    int pos = 0;
-#pragma unroll
-    for (int width = 16; width >= 1; width >>= 1) {
-        const int32_t c = __popc(v & ((1u << width) - 1u));
-        if (c <= n) {
-            n -= c;
-            v >>= width;
-            pos += width;
-        }
-    }
-    return pos;
-}
-
 // 2b: the walk (one warp), 32 candidates per batch, one per lane, in sweep order from the
 // hand. Misses are consumed in position order, so the m-th consumed miss is the m-th set bit
 // of the final miss queue: the walk records miss numbers, and a parallel pass afterwards turns

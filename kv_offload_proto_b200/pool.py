@@ -216,6 +216,21 @@ class DevicePool:
             injective=self.injective, path=path)
         return status
 
+    def batch_write(self, layer_id, topk_indices, req_pool_indices, req_host_base, topk_device_slots, export_flags,
+                    num_real, hot_row_base, max_num_reqs, top_k, stream=0, block_dim=1, *, hot_req_stride_rows=0) -> int:
+        """Export one layer's flagged hot rows to their pool rows (kvc_scatter_rows, the single-layer
+        decode-increment export of doc/kv_offload_design.md:394-396): batch_read's arguments and
+        rules in the opposite direction, one launch per segment. Returns the status address."""
+        status = self.next_status()
+        off = layer_id * self.per_layer_seg_rows
+        a = [_ptr(topk_indices), _ptr(req_pool_indices), _ptr(req_host_base), _ptr(topk_device_slots),
+             _ptr(export_flags), _ptr(num_real), _ptr(hot_row_base)]
+        for s in range(self.node_num):
+            self._k.export_seg(self.channels[s], self.seg_bases[s], off, self.per_layer_seg_rows, self.row_bytes, *a,
+                               top_k, max_num_reqs, self.stripe_rows, self.node_num, s, status, stream, block_dim,
+                               hot_req_stride_rows=hot_req_stride_rows, injective=self.injective)
+        return status
+
     def batch_write_alllayers(self, row_lo, row_cnt, src_layer0_base, src_layer_stride, stream=0, block_dim=1) -> int:
         """Export rows [row_lo, row_lo+row_cnt) of every layer to their segments
         (xds_ems_pool.py:220-230): one launch per segment, as in the reference."""

@@ -14,6 +14,7 @@
  *   ko_sieve_ht_init       kvops/kernel/hisp_sieve_ht_init.cpp:14-60
  *   ko_gather_rows         kvops/kernel/kvc_gather_rows.cpp:12-96
  *   ko_export_alllayer     kvops/kernel/kvc_scatter_rows_alllayer.cpp:11-67
+ *   ko_scatter_rows        doc/kv_offload_design.md:394-396 (gather rules, opposite direction)
  *   ko_node_of/ko_seg_row  kvops/kernel/kvc_common.h:81-89, common/kv_layout.h:26-39
  *   ko_ht_size             kvops/kvops_ext/kvops_ext.cpp:297-300
  *
@@ -286,6 +287,39 @@ int64_t ko_gather_rows(uint8_t *seg_base, uint32_t layer_offset_rows, uint32_t r
         const uint8_t *src = seg_base + ((uint64_t)layer_offset_rows + seg_row) * row_bytes;
         const int64_t dst_row = hot_req_stride_rows > 0 ? req * hot_req_stride_rows + slot : slot;
         memcpy(hot_base + (uint64_t)dst_row * row_bytes, src, row_bytes);
+        queued++;
+    }
+    return queued;
+}
+
+/* Host restatement of kvc_scatter_rows, the single-layer indexed export of decode
+ * increments (doc/kv_offload_design.md:394-396: the arguments of kvc_gather_rows with the data
+ * moving hot rows -> segment; the reference deleted its implementation, :544). The selection
+ * rules are the gather's (kvc_gather_rows.cpp:54-76) with export_flags in place of is_miss. */
+int64_t ko_scatter_rows(uint8_t *seg_base, uint32_t layer_offset_rows, uint32_t row_bytes,
+                        const int32_t *topk, const int64_t *req_pool, const int64_t *host_base,
+                        const int32_t *slots, const int8_t *export_flags, int32_t num_real,
+                        const uint8_t *hot_base, uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe,
+                        uint32_t nodes, uint32_t my_node, int64_t hot_req_stride_rows, int injective)
+{
+    if (num_real > (int32_t)max_num_reqs) num_real = (int32_t)max_num_reqs;
+    const int64_t total = (int64_t)num_real * top_k;
+    int64_t queued = 0;
+    for (int64_t pos = 0; pos < total; pos++) {
+        if (export_flags[pos] == 0) continue;
+        const int64_t bid = pos / top_k;
+        const int32_t t = topk[pos];
+        const int32_t slot = slots[pos];
+        if (t < 0 || slot < 0) continue;
+        const int64_t req = req_pool[bid];
+        if (req < 0) continue;
+        const uint32_t row = (uint32_t)(host_base[bid] + t);
+        if (ko_node_of(row, stripe, nodes) != my_node) continue;
+        const uint64_t seg_row =
+            injective ? ko_seg_row_injective(row, stripe, nodes) : ko_seg_row(row, stripe, nodes);
+        const int64_t src_row = hot_req_stride_rows > 0 ? req * hot_req_stride_rows + slot : slot;
+        memcpy(seg_base + ((uint64_t)layer_offset_rows + seg_row) * row_bytes,
+               hot_base + (uint64_t)src_row * row_bytes, row_bytes);
         queued++;
     }
     return queued;

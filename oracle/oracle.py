@@ -18,7 +18,7 @@ _lib = None
 __all__ = [
     "lib", "ht_size", "align", "hash32", "node_of", "seg_row_of", "seg_row_injective", "per_layer_seg_rows",
     "per_layer_seg_rows_injective", "seg_offset", "SieveState", "sieve_update", "gather_rows", "gather_all",
-    "export_alllayer", "ref_layout_lib", "build",
+    "export_alllayer", "scatter_rows", "ref_layout_lib", "build",
 ]
 
 
@@ -54,6 +54,9 @@ def lib():
         L.ko_gather_all.argtypes = [P, u32, u32, P, P, P, P, P, i32, P, u32, u32, u32, u32, i64, ctypes.c_int,
                                     i32]
         L.ko_gather_all.restype = i64
+        L.ko_scatter_rows.argtypes = [P, u32, u32, P, P, P, P, P, i32, P, u32, u32, u32, u32, u32, i64,
+                                      ctypes.c_int]
+        L.ko_scatter_rows.restype = i64
         L.ko_export_alllayer.argtypes = [P, u32, u32, u32, u32, u32, P, u64, u32, u32, u32, ctypes.c_int]
         L.ko_export_alllayer.restype = i64
         _lib = L
@@ -193,6 +196,14 @@ def gather_rows(seg, layer_offset_rows, row_bytes, topk, req_pool, host_base, sl
     return int(lib().ko_gather_rows(_p(seg), layer_offset_rows, row_bytes, _p(topk), _p(req_pool),
                                     _p(host_base), _p(slots), _p(is_miss), num_real, _p(hot), top_k,
                                     max_num_reqs, stripe, nodes, my_node, hot_req_stride_rows, int(injective)))
+
+
+def scatter_rows(seg, layer_offset_rows, row_bytes, topk, req_pool, host_base, slots, export_flags, num_real, hot,
+                 top_k, max_num_reqs, stripe, nodes, my_node, hot_req_stride_rows=0, injective=False):
+    """One export_seg (kvc_scatter_rows) launch on host byte arrays (seg modified in place)."""
+    return int(lib().ko_scatter_rows(_p(seg), layer_offset_rows, row_bytes, _p(topk), _p(req_pool),
+                                     _p(host_base), _p(slots), _p(export_flags), num_real, _p(hot), top_k,
+                                     max_num_reqs, stripe, nodes, my_node, hot_req_stride_rows, int(injective)))
 
 
 def gather_all(segs, layer_offset_rows, row_bytes, topk, req_pool, host_base, slots, is_miss, num_real, hot,
