@@ -508,6 +508,7 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
                 for (int b = 0; b < 6; ++b) c += __popc(bs[b] & lanes) << b;
                 return c;
             };
+            const int32_t e_me = before((1u << lane) - 1u);  // misses in the window's words before mine
             const int32_t avail = before(kAll) - s0;
             if (avail <= 0) {  // every miss in these 32 words is consumed
                 if (w0 + 32 >= qwords) {
@@ -519,7 +520,6 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
                 continue;
             }
             if (avail < 32 && w0 + 32 < qwords) {  // move up to the word of the next unconsumed miss
-                const int32_t e_me = before((1u << lane) - 1u);
                 const int ls = __ffs(__ballot_sync(kAll, e_me + static_cast<int32_t>(pop) > s0)) - 1;
                 if (ls > 0) {
                     s0 -= __shfl_sync(kAll, e_me, ls);
@@ -532,12 +532,13 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
             const int32_t wf = f == kNone16 ? 32 : static_cast<int32_t>(f >> 5) - w0;
             const int src = wf < 0 ? 0 : (wf > 31 ? 31 : wf);
             const uint32_t ws = __shfl_sync(kAll, W, src);
+            const int32_t es = __shfl_sync(kAll, e_me, src);
             int32_t tj = 0;
             if (live) {
                 if (wf >= 32) {
                     tj = mw;
                 } else if (wf >= 0) {
-                    const int32_t r = before((1u << src) - 1u) + __popc(ws & ((1u << (f & 31)) - 1u)) - s0;
+                    const int32_t r = es + __popc(ws & ((1u << (f & 31)) - 1u)) - s0;
                     tj = r < 0 ? 0 : (r > mw ? mw : r);
                 }
             }
@@ -560,7 +561,8 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
             if (cmin != 0xFFFFFFFFu) {
                 const int32_t wc = static_cast<int32_t>(cmin >> 5) - w0;  // >= 0: cmin follows a reached miss
                 const uint32_t wcs = __shfl_sync(kAll, W, wc < 32 ? wc : 0);
-                if (wc < 32) rc = before((1u << wc) - 1u) + __popc(wcs & ((1u << (cmin & 31)) - 1u)) - s0;
+                const int32_t ecs = __shfl_sync(kAll, e_me, wc < 32 ? wc : 0);
+                if (wc < 32) rc = ecs + __popc(wcs & ((1u << (cmin & 31)) - 1u)) - s0;
             }
             const bool com = reached && myk < rc;
             const uint32_t cm = __ballot_sync(kAll, com);
