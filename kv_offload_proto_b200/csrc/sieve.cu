@@ -859,6 +859,31 @@ __device__ __forceinline__ void compute_sync()
         __syncthreads();
 }
 
+// compute_sync that also returns whether any compute thread passed true.
+template <bool kFused>
+__device__ __forceinline__ bool compute_sync_or(bool v)
+{
+    if (!kFused) return __syncthreads_or(v) != 0;
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(kFastThreads)
+        : "memory");
+    return r != 0;
+}
+
+// Warp-aggregated append: the index of this lane's item in a shared list counted by *n (all
+// 32 lanes call it; lanes with want == false get an unused index).
+__device__ __forceinline__ int warp_append(int32_t *n, bool want)
+{
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, want);
+    const int lane = threadIdx.x & 31;
+    int at = 0;
+    if (lane == 0 && bal) at = atomicAdd(n, __popc(bal));
+    return __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(bal & ((1u << lane) - 1u));
+}
+
 // ---- cooperative layer-step: ready words and copy helpers ----
 
 // Publishes that request `bid`'s slots and miss flags are in global memory (after a barrier
@@ -1058,12 +1083,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         return;
     }
     __shared__ int s_flag;     // nonzero: recompute this step with the sequential path
-    __shared__ int s_changed[2];  // per-round progress flags, used alternately
     __shared__ int s_any_miss;
     __shared__ int32_t s_hand;
     __shared__ bool s_dirty;
     __shared__ int32_t s_warp[32];
-    __shared__ int32_t s_ncand, s_last, s_nkeys, s_n0, s_nvis;
+    __shared__ int32_t s_ncand, s_last, s_nkeys, s_ndel, s_n0, s_nvis;
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -1134,7 +1158,6 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         s_hand = hand;
         s_flag = 0;
         s_any_miss = 0;
-        s_changed[0] = s_changed[1] = 0;
     }
     cp_async_wait_all();
     __syncthreads();
@@ -1325,120 +1348,126 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     }
 
     // ---- phase 4: delete the evicted tokens from the table, re-packing each probe run ----
+    // Every miss took exactly one evicted slot (s_os), so the misses list the deletions; the
+    // passes below visit only the listed cells, never the whole table.
     const bool update_table = !s_flag && s_any_miss;
-    if (update_table) {
-        for (int32_t c = tid; c < dbs; c += ntc) {
-            if (s_evt[c] == kNone16 || s_tok[c] < 0) continue;
-            uint32_t idx = ht_hash(s_tok[c]) & mask;
-            for (uint32_t n = 0; n <= mask; ++n) {
-                if (s_ht[idx] == static_cast<uint16_t>(c + 1)) {
-                    s_ht[idx] = kDelMark;
-                    break;
-                }
-                idx = (idx + 1) & mask;
-            }
-        }
-    }
-    compute_sync<kFused>();
-    if (update_table) {  // the first deleted cell of each run leads its re-pack
-        for (uint32_t i = tid; i <= mask; i += ntc) {
-            if (s_ht[i] != kDelMark) continue;
-            uint32_t j = (i - 1) & mask;
-            bool lead = true;
-            for (uint32_t n = 0; n <= mask; ++n) {
-                const uint16_t e = s_ht[j];
-                if (e == kHtEmpty) break;
-                if (e == kDelMark || e == kLeadMark) {
-                    lead = false;
-                    break;
-                }
-                j = (j - 1) & mask;
-            }
-            if (lead) s_ht[i] = kLeadMark;
-        }
-    }
-    compute_sync<kFused>();
-    if (update_table) {
-        for (uint32_t i = tid; i <= mask; i += ntc) {
-            if (s_ht[i] != kLeadMark) continue;
-            // Walk the run from its first deleted cell; every surviving entry moves to the
-            // first empty cell from its home, which is never past its old cell.
-            uint32_t e = i;
-            for (uint32_t n = 0; n <= mask; ++n) {
-                const uint16_t v = s_ht[e];
-                if (v == kHtEmpty) break;
-                s_ht[e] = kHtEmpty;
-                if (v != kDelMark && v != kLeadMark) {
-                    uint32_t q = ht_hash(tok_of(s_tok, v, padded)) & mask;
-                    for (uint32_t m = 0; m <= mask && s_ht[q] != kHtEmpty; ++m) q = (q + 1) & mask;
-                    s_ht[q] = v;
-                }
-                e = (e + 1) & mask;
-            }
-        }
-    }
-    compute_sync<kFused>();
-
-    // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
     uint16_t *s_keys = reinterpret_cast<uint16_t *>(smem + L.dkey);  // candidate list no longer needed
+    uint16_t *s_dl = s_keys + K;                                      // table cells deleted this step
     if (update_table) {
-        if (tid == 0) s_nkeys = 0;
+        if (tid == 0) {
+            s_nkeys = 0;
+            s_ndel = 0;
+        }
         compute_sync<kFused>();
         for (int32_t m0 = 0; m0 < K; m0 += ntc) {  // list the misses (warp-aggregated appends)
             const int32_t m = m0 + tid;
             const bool is_key = m < K && ((s_missb[m >> 5] >> (m & 31)) & 1u);
-            const unsigned bal = __ballot_sync(0xFFFFFFFFu, is_key);
-            int at = 0;
-            if ((tid & 31) == 0 && bal) at = atomicAdd(&s_nkeys, __popc(bal));
-            at = __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(bal & ((1u << (tid & 31)) - 1u));
+            const int at = warp_append(&s_nkeys, is_key);
             if (is_key) {
                 s_keys[at] = static_cast<uint16_t>(m);
                 s_aux[m] = static_cast<uint16_t>(ht_hash(s_topk[m]) & mask);
                 s_cls[m] = kClsPending;
             }
         }
+        compute_sync<kFused>();
+        const int32_t nkeys = s_nkeys;
+        for (int32_t j0 = 0; j0 < nkeys; j0 += ntc) {  // mark the evicted entries, listing their cells
+            const int32_t j = j0 + tid;
+            bool del = false;
+            uint32_t idx = 0;
+            if (j < nkeys) {
+                const int32_t c = s_os[s_keys[j]];
+                if (s_evt[c] != kNone16 && s_tok[c] >= 0) {
+                    idx = ht_hash(s_tok[c]) & mask;
+                    for (uint32_t n = 0; n <= mask; ++n) {
+                        if (s_ht[idx] == static_cast<uint16_t>(c + 1)) {
+                            s_ht[idx] = kDelMark;
+                            del = true;
+                            break;
+                        }
+                        idx = (idx + 1) & mask;
+                    }
+                }
+            }
+            const int at = warp_append(&s_ndel, del);
+            if (del) s_dl[at] = static_cast<uint16_t>(idx);
+        }
     }
     compute_sync<kFused>();
+    const int32_t ndel = update_table ? s_ndel : 0;
+    for (int32_t j = tid; j < ndel; j += ntc) {  // the first deleted cell of each run leads its re-pack
+        const uint32_t i = s_dl[j];
+        uint32_t q = (i - 1) & mask;
+        bool lead = true;
+        for (uint32_t n = 0; n <= mask; ++n) {
+            const uint16_t e = s_ht[q];
+            if (e == kHtEmpty) break;
+            if (e == kDelMark || e == kLeadMark) {
+                lead = false;
+                break;
+            }
+            q = (q - 1) & mask;
+        }
+        if (lead) s_ht[i] = kLeadMark;
+    }
+    compute_sync<kFused>();
+    for (int32_t j = tid; j < ndel; j += ntc) {
+        const uint32_t i = s_dl[j];
+        if (s_ht[i] != kLeadMark) continue;
+        // Walk the run from its first deleted cell; every surviving entry moves to the first
+        // empty cell from its home, which is never past its old cell.
+        uint32_t e = i;
+        for (uint32_t n = 0; n <= mask; ++n) {
+            const uint16_t v = s_ht[e];
+            if (v == kHtEmpty) break;
+            s_ht[e] = kHtEmpty;
+            if (v != kDelMark && v != kLeadMark) {
+                uint32_t q = ht_hash(tok_of(s_tok, v, padded)) & mask;
+                for (uint32_t m = 0; m <= mask && s_ht[q] != kHtEmpty; ++m) q = (q + 1) & mask;
+                s_ht[q] = v;
+            }
+            e = (e + 1) & mask;
+        }
+    }
+    compute_sync<kFused>();
+
+    // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
+    // One pass per round: a placed key first checks that it still owns its cell (a displaced
+    // one moves on), a pending key then tries its current cell. The round's barrier ORs the
+    // progress flags; a round without a pending or displaced key leaves the table final.
     if (update_table) {
         const int32_t nkeys = s_nkeys;
         const int32_t limit = 4 * p.ht_size + 64;
         for (int32_t round = 0;; ++round) {
-            // Round r raises s_changed[r & 1]; thread 0 clears the other flag once every thread
-            // has passed the first barrier of round r, i.e. after all reads of round r-1's flag.
             bool ch = false;
             for (int32_t j = tid; j < nkeys; j += ntc) {
                 const int32_t m = s_keys[j];
-                if (s_cls[m] != kClsPending) continue;
                 const uint16_t entry = static_cast<uint16_t>(s_os[m] + 1);
-                const uint32_t at = s_aux[m];
-                const uint16_t e = s_ht[at];
+                uint8_t cls = s_cls[m];
+                uint32_t at = s_aux[m];
+                if (cls == kClsPlaced && s_ht[at] != entry) {  // displaced by an earlier miss
+                    cls = kClsPending;
+                    at = (at + 1) & mask;
+                }
+                if (cls != kClsPending) continue;
                 ch = true;
+                const uint16_t e = s_ht[at];
                 if (e == kHtEmpty) {
                     if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), kHtEmpty, entry) == kHtEmpty)
-                        s_cls[m] = kClsPlaced;
+                        cls = kClsPlaced;
                 } else {
                     const int32_t es = static_cast<int32_t>(e) - 1;
                     const uint16_t te = es < padded ? s_evt[es] : kNone16;
                     if (te == kNone16 || te < m) {
-                        s_aux[m] = static_cast<uint16_t>((at + 1) & mask);
+                        at = (at + 1) & mask;
                     } else if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), e, entry) == e) {
-                        s_cls[m] = kClsPlaced;  // the later miss it displaced moves on
+                        cls = kClsPlaced;  // the later miss it displaced moves on
                     }
                 }
+                s_cls[m] = cls;
+                s_aux[m] = static_cast<uint16_t>(at);
             }
-            compute_sync<kFused>();
-            if (tid == 0) s_changed[(round + 1) & 1] = 0;
-            for (int32_t j = tid; j < nkeys; j += ntc) {
-                const int32_t m = s_keys[j];
-                if (s_cls[m] == kClsPlaced && s_ht[s_aux[m]] != static_cast<uint16_t>(s_os[m] + 1)) {
-                    s_cls[m] = kClsPending;
-                    s_aux[m] = static_cast<uint16_t>((s_aux[m] + 1) & mask);
-                    ch = true;
-                }
-            }
-            if (ch) s_changed[round & 1] = 1;
-            compute_sync<kFused>();
-            if (!s_changed[round & 1]) break;
+            if (!compute_sync_or<kFused>(ch)) break;
             if (round > limit) {  // cannot happen on a table at load <= 0.5; recompute if it does
                 if (tid == 0) s_flag = 1;
                 compute_sync<kFused>();
