@@ -45,11 +45,16 @@ struct DeviceState {
     int sm_count = 0;
     uint32_t *ready = nullptr;  // cooperative layer-steps: kReadyBlocks blocks of kReadyWords words
     std::atomic<uint32_t> ready_next{0};
+    uint2 *wl = nullptr;         // cooperative layer-steps: kWalkListBufs walk-list buffers
+    size_t wl_entries = 0;       // entries per buffer
+    std::vector<uint2 *> wl_old;  // outgrown buffers (a captured graph may still name one)
 };
 
-// Ready words of cooperative layer-steps: launch n uses block n % kReadyBlocks, so a block is
-// reused only after kReadyBlocks later launches; the kernel keeps each block's epoch itself.
-constexpr uint32_t kReadyBlocks = 4096, kReadyWords = 256;
+// Words of cooperative layer-steps: launch n uses block n % kReadyBlocks, so a block is reused
+// only after kReadyBlocks later launches; the kernel keeps each block's epoch itself. Launch n
+// also uses walk-list buffer n % kWalkListBufs: cooperative launches fill the device, so no
+// more than two consecutive ones are ever resident together.
+constexpr uint32_t kReadyBlocks = 1024, kReadyWords = kvb::kCoopBlockWords, kWalkListBufs = 4;
 
 std::mutex g_mu;
 thread_local uint32_t t_last_step_path = KVOPS_STEP_AUTO;  // path the last kvops_sieve_import ran
@@ -358,13 +363,31 @@ int ensure_ready_words(DeviceState *ds)
     return KVOPS_OK;
 }
 
-// The ready words for the next cooperative layer-step on this device.
-int next_ready_block(DeviceState *ds, uint32_t **words)
+// Grows (once per shape, never shrinking) the walk-list buffers to `entries` entries each.
+int ensure_walk_lists(DeviceState *ds, size_t entries)
 {
-    const int rc = ensure_ready_words(ds);
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ds->wl != nullptr && ds->wl_entries >= entries) return KVOPS_OK;
+    uint2 *w = nullptr;
+    cudaError_t e = cudaMalloc(&w, sizeof(uint2) * entries * kWalkListBufs);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(walk lists)");
+    if (ds->wl != nullptr) ds->wl_old.push_back(ds->wl);
+    ds->wl = w;
+    ds->wl_entries = entries;
+    return KVOPS_OK;
+}
+
+// The block of words and the walk-list buffer (max_num_reqs x top_k entries) for the next
+// cooperative layer-step on this device.
+int next_ready_block(DeviceState *ds, size_t wl_entries, uint32_t **words, uint2 **wl)
+{
+    int rc = ensure_ready_words(ds);
+    if (rc != KVOPS_OK) return rc;
+    rc = ensure_walk_lists(ds, wl_entries);
     if (rc != KVOPS_OK) return rc;
     const uint32_t n = ds->ready_next.fetch_add(1, std::memory_order_relaxed);
     *words = ds->ready + static_cast<size_t>(n % kReadyBlocks) * kReadyWords;
+    *wl = ds->wl + static_cast<size_t>(n % kWalkListBufs) * ds->wl_entries;
     return KVOPS_OK;
 }
 
@@ -440,6 +463,8 @@ int kvops_close(void)
         cudaSetDevice(kv.first);
         cudaFree(kv.second->ring);
         if (kv.second->ready) cudaFree(kv.second->ready);
+        if (kv.second->wl) cudaFree(kv.second->wl);
+        for (uint2 *w : kv.second->wl_old) cudaFree(w);
         delete kv.second;
     }
     g_devices.clear();
@@ -654,10 +679,11 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (sds != nullptr && (path == KVOPS_STEP_AUTO || path == KVOPS_STEP_COOP) && vec16_ok(gp)) {
         uint32_t *words = nullptr;
-        rc = next_ready_block(sds, &words);
+        uint2 *wl = nullptr;
+        rc = next_ready_block(sds, static_cast<size_t>(max_num_reqs) * top_k, &words, &wl);
         if (rc != KVOPS_OK) return rc;
         bool launched = false;
-        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, st, &launched);
+        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, wl, st, &launched);
         if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import (cooperative)");
         if (launched) {
             t_last_step_path = KVOPS_STEP_COOP;
@@ -695,6 +721,8 @@ int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t pad
     int rc = current_device_state(&ds);
     if (rc != KVOPS_OK) return rc;
     rc = ensure_ready_words(ds);
+    if (rc != KVOPS_OK) return rc;
+    rc = ensure_walk_lists(ds, static_cast<size_t>(max_num_reqs) * top_k);
     if (rc != KVOPS_OK) return rc;
     int64_t ht_size = 1024;
     while (ht_size < 2 * (static_cast<int64_t>(padded_buffer_size) + top_k)) ht_size <<= 1;

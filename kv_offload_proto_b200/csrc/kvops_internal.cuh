@@ -100,12 +100,16 @@ struct ExportParams {
 };
 
 // Extra arguments of the layer-step kernels (sieve.cu).
+// Words of one cooperative layer-step's claim / queue / progress block (layout in sieve.cu).
+constexpr uint32_t kCoopBlockWords = 2048;
+
 struct StepExtra {
     int32_t nsl;        // copy warp: sets of 32 ring slots
     uint32_t ring_off;  // copy warp: byte offset of the ring in dynamic shared memory
-    uint32_t *flags;    // cooperative step: the launch's block of 256 ready words
+    uint32_t *flags;    // cooperative step: the launch's block of kCoopBlockWords words
     uint32_t epoch;     // cooperative step: set in the kernel from the block (host passes 0)
     uint32_t magic;     // copy helpers: multiply-high constant of cta_copy_rows (0: divide)
+    uint2 *wl;          // cooperative step: the launch's walk lists, max_num_reqs x top_k entries
 };
 
 // Publishes completion: called by thread 0 of every CTA after a __syncthreads() that
@@ -161,7 +165,7 @@ cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cud
 // other launch uses while this one runs) and every other CTA resident on the GPU copies miss
 // rows of ready requests. *launched = false (nothing launched) when fewer than 8 copy CTAs fit
 // beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
-cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl, cudaStream_t s,
                               bool *launched);
 // Sets up, without launching, what the first cooperative step of this shape would: the
 // kernel's shared-memory limit and the cached residency (so a later call may be captured).

@@ -19,22 +19,23 @@ __device__ __forceinline__ uint8_t load_stream<uint8_t>(const uint8_t *p)
     return *reinterpret_cast<const volatile uint8_t *>(p);
 }
 
-// Copies n rows (src[i] -> dst[i]) of `row_bytes` with the whole CTA: the rows form one flat
-// array of V-sized chunks split evenly over the threads, kUnroll loads in flight per thread
-// before the matching stores. `magic` = ceil(2^32 / chunks_per_row) when exact division by
-// multiply-high is valid for every chunk index (host-checked), else 0.
+// Copies n rows (src[i] -> dst[i]) of `row_bytes` with threads [0, nthreads) of a group (gt:
+// this thread's index in it): the rows form one flat array of V-sized chunks split evenly over
+// the threads, kUnroll loads in flight per thread before the matching stores. `magic` =
+// ceil(2^32 / chunks_per_row) when exact division by multiply-high is valid for every chunk
+// index (host-checked), else 0.
 template <typename V, int kUnroll>
-__device__ __forceinline__ void cta_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
-                                              uint32_t row_bytes, uint32_t magic)
+__device__ __forceinline__ void group_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
+                                                uint32_t row_bytes, uint32_t magic, uint32_t gt, uint32_t nthreads)
 {
     const uint32_t cpr = row_bytes / sizeof(V);
     const uint32_t total = static_cast<uint32_t>(n) * cpr;
-    for (uint32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * kUnroll) {
+    for (uint32_t i0 = gt; i0 < total; i0 += nthreads * kUnroll) {
         V v[kUnroll];
         uint32_t rr[kUnroll], cc[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const uint32_t i = i0 + u * blockDim.x;
+            const uint32_t i = i0 + u * nthreads;
             const uint32_t r = magic ? __umulhi(i, magic) : i / cpr;
             rr[u] = r;
             cc[u] = i - r * cpr;
@@ -42,9 +43,17 @@ __device__ __forceinline__ void cta_copy_rows(const uint8_t *const *src, uint8_t
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            if (i0 + u * blockDim.x < total) reinterpret_cast<V *>(dst[rr[u]])[cc[u]] = v[u];
+            if (i0 + u * nthreads < total) reinterpret_cast<V *>(dst[rr[u]])[cc[u]] = v[u];
         }
     }
+}
+
+// The same with the whole CTA.
+template <typename V, int kUnroll>
+__device__ __forceinline__ void cta_copy_rows(const uint8_t *const *src, uint8_t *const *dst, int n,
+                                              uint32_t row_bytes, uint32_t magic)
+{
+    group_copy_rows<V, kUnroll>(src, dst, n, row_bytes, magic, threadIdx.x, blockDim.x);
 }
 
 // The gather rule for flat position `pos` (= batch row * top_k + k) of one layer

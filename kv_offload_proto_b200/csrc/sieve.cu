@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(kSieveThreads) sieve_ht_init_kernel(const HtIn
 // written back and is recomputed by the sequential path from the untouched global state.
 
 constexpr int kFastThreads = 512;
+constexpr int kHelpBatch = 256;  // numbers per walk-list batch (cooperative step)
 
 constexpr uint16_t kNone16 = 0xFFFFu;
 constexpr uint16_t kDelMark = 0xFFFFu;   // table cell: deleted entry (entries are <= 65520)
@@ -355,7 +356,7 @@ constexpr uint16_t kLeadMark = 0xFFFEu;  // table cell: first deleted entry of i
 constexpr uint8_t kClsNone = 0, kClsRes = 1, kClsNew = 2, kClsPending = 3, kClsPlaced = 4;
 
 struct FastLayout {
-    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, posl, missb, wofs, total;
+    size_t ht, tok, topk, os, om, cls, aux, tf, evt, vini, vfin, dkey, dfirst, posl, missb, wofs, nslot, hpos, total;
     int32_t dcap;
 };
 
@@ -392,6 +393,8 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
     L.posl = L.dkey + cl;
     L.missb = take(&o, 4ull * ((K + 31) / 32));
     L.wofs = take(&o, 4ull * ((dbs + 31) / 32 + 1));
+    L.nslot = take(&o, 2ull * K);         // miss number -> slot (cooperative step)
+    L.hpos = take(&o, 2ull * kHelpBatch);  // walk-list batch: positions
     L.total = o;
     return L;
 }
@@ -475,8 +478,10 @@ __device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint3
 // word of the next unconsumed miss (at most once per commit), which bounds the rounds.
 // Returns false when the sweep would pass a slot twice (misses remain after every candidate),
 // or if the bound were ever exceeded. *nvis_out: candidates visited (a prefix of sweep order).
+// nslot (optional): nslot[m] = the slot evicted for miss number m; prog (optional): prog[0] =
+// misses consumed so far, published after each round (numbers below it are final).
 __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t *evt, uint32_t *missb, int32_t K,
-                                int32_t *last_out, int32_t *nvis_out)
+                                int32_t *last_out, int32_t *nvis_out, uint16_t *nslot, int32_t *prog)
 {
     const unsigned kAll = 0xFFFFFFFFu;
     const int lane = threadIdx.x & 31;
@@ -573,6 +578,7 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
                 cand[my] = (num << 16) | slot;
                 if (ev) {
                     evt[slot] = static_cast<uint16_t>(num);
+                    if (nslot != nullptr) nslot[num] = static_cast<uint16_t>(slot);
                     if (f != kNone16) atomicOr(&missb[f >> 5], 1u << (f & 31));  // created miss
                 }
             }
@@ -584,6 +590,10 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
             cur = 32 - __clz(cm);
             nvis = sb + cur;
             __syncwarp();  // created misses visible before the next round reads the queue
+            if (prog != nullptr && ec > 0 && lane == 0) {
+                __threadfence_block();
+                *reinterpret_cast<volatile int32_t *>(prog) = G;
+            }
         }
     }
     if (!done) {  // every candidate was visited: unconsumed misses mean the sweep would wrap
@@ -886,14 +896,6 @@ __device__ __forceinline__ int warp_append(int32_t *n, bool want)
 
 // ---- cooperative layer-step: ready words and copy helpers ----
 
-// Publishes that request `bid`'s slots and miss flags are in global memory (after a barrier
-// that follows their stores).
-__device__ __forceinline__ void raise_ready(const StepExtra &x, int32_t bid)
-{
-    __threadfence();
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(x.flags + bid), "r"(x.epoch) : "memory");
-}
-
 // Waits for a ready word; false after ~2^24 polls (more than a second).
 __device__ __forceinline__ bool wait_ready(const uint32_t *f, uint32_t epoch)
 {
@@ -906,19 +908,28 @@ __device__ __forceinline__ bool wait_ready(const uint32_t *f, uint32_t epoch)
     return false;
 }
 
-// Layout of a launch's block of 256 ready words: [0, kMaxCoopReqs) one per request; copy items
-// are claimed with one atomicAdd on kClaimWord, which SIEVE CTA 0 zeroes at kernel entry before
-// it sets kClaimInit to the epoch (every CTA waits for that once before its first claim, so a
-// count left by an older launch is never used). The epoch itself lives on the device: every
-// CTA reads kEpochWord at entry and uses its value + 1; the last CTA to finish (kArriveWord)
-// stores that value back. A launch replayed from a CUDA graph therefore gets a new epoch each
-// time without any host work.
+// Layout of a launch's block of kCoopBlockWords words. Copy items are claimed with one atomicAdd on
+// kClaimWord; SIEVE CTA 0 zeroes it and kQueueTail at kernel entry before it sets kClaimInit to
+// the epoch (every CTA waits for that once before its first claim, so a count left by an older
+// launch is never used). Requests enter a ready queue in the order their outputs become final:
+// a SIEVE CTA takes the next slot (kQueueTail) and publishes (epoch << 32) | request in it;
+// item i covers part i % parts of the request in slot i / parts, so the copy follows the order
+// in which requests become ready. While a request's walk runs, its walk list (StepExtra::wl)
+// receives one entry per miss number the walk has made final, and kProgBase + 2 r publishes
+// (epoch << 32) | (entries << 1) | final; copy CTAs copy those rows during the walk. The epoch
+// itself lives on the device: every CTA reads kEpochWord at entry and uses its value + 1; the
+// last CTA to finish (kArriveWord) stores that value back. A launch replayed from a CUDA graph
+// therefore gets a new epoch each time without any host work.
 constexpr int kClaimInit = 252, kClaimWord = 253, kArriveWord = 254, kEpochWord = 255, kMaxCoopReqs = 252;
+constexpr int kQueueTail = 256, kQueueBase = 512;  // kMaxCoopReqs 64-bit slots from word 512
+constexpr int kProgBase = 1024;                     // kMaxCoopReqs 64-bit progress words
+static_assert(kProgBase + 2 * kMaxCoopReqs <= static_cast<int>(kCoopBlockWords), "block layout");
 constexpr int kCoopUnroll = 12;  // 16-byte loads in flight per thread of a copy CTA
 
 __device__ __forceinline__ void init_claims(const StepExtra &x)
 {
     *reinterpret_cast<volatile uint32_t *>(x.flags + kClaimWord) = 0u;
+    *reinterpret_cast<volatile uint32_t *>(x.flags + kQueueTail) = 0u;
     __threadfence();
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(x.flags + kClaimInit), "r"(x.epoch) : "memory");
 }
@@ -933,6 +944,67 @@ __device__ __forceinline__ int64_t claim_item(const StepExtra &x, bool *inited)
     return static_cast<int64_t>(atomicAdd(x.flags + kClaimWord, 1u));
 }
 
+// The next ready-queue slot; the caller has seen kClaimInit hold this epoch.
+__device__ __forceinline__ int32_t queue_claim(const StepExtra &x)
+{
+    return static_cast<int32_t>(atomicAdd(x.flags + kQueueTail, 1u));
+}
+
+// Publishes request r in ready-queue slot k: its slots and miss flags are in global memory
+// (called after a barrier that follows their stores), and its miss rows at positions below
+// pw (0..top_k) are already copied. k < 0: the claim failed; nothing is published and the
+// copy helpers time out on the slot (KVOPS_ERR_COPY_TIMEOUT).
+__device__ __forceinline__ void queue_publish(const StepExtra &x, int32_t k, int32_t r, int32_t pw)
+{
+    if (k < 0 || k >= kMaxCoopReqs) return;
+    __threadfence();
+    const uint64_t v = (static_cast<uint64_t>(x.epoch) << 32) | (static_cast<uint32_t>(pw) << 8) |
+                       static_cast<uint32_t>(r);
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(x.flags + kQueueBase + 2 * k), "l"(v) : "memory");
+}
+
+// Claims a slot (waiting for kClaimInit first) and publishes request r in it (pw as above).
+__device__ __forceinline__ void queue_claim_publish(const StepExtra &x, int32_t r, int32_t pw = 0)
+{
+    queue_publish(x, wait_ready(x.flags + kClaimInit, x.epoch) ? queue_claim(x) : -1, r, pw);
+}
+
+// Ready-queue slot k for this epoch: (pw << 8) | request, or -1 while it is not published.
+__device__ __forceinline__ int32_t queue_probe(const StepExtra &x, int64_t k)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(x.flags + kQueueBase + 2 * k) : "memory");
+    return static_cast<uint32_t>(v >> 32) == x.epoch ? static_cast<int32_t>(static_cast<uint32_t>(v) & 0x7FFFFFFFu) : -1;
+}
+
+// Waits for ready-queue slot k; -1 after ~2^24 polls (more than a second).
+__device__ __forceinline__ int32_t queue_wait(const StepExtra &x, int64_t k)
+{
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        const int32_t r = queue_probe(x, k);
+        if (r >= 0) return r;
+        __nanosleep(64);
+    }
+    return -1;
+}
+
+// Publishes that request r's walk list holds `entries` entries (final: no more will come).
+// The caller's entry stores are fenced (gpu scope) before this.
+__device__ __forceinline__ void wl_publish(const StepExtra &x, int32_t r, int32_t entries, bool final)
+{
+    const uint64_t v = (static_cast<uint64_t>(x.epoch) << 32) | (static_cast<uint32_t>(entries) << 1) |
+                       (final ? 1u : 0u);
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(x.flags + kProgBase + 2 * r), "l"(v) : "memory");
+}
+
+// Request r's walk-list progress this epoch: (entries << 1) | final, or -1 before any.
+__device__ __forceinline__ int32_t wl_probe(const StepExtra &x, int32_t r)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(x.flags + kProgBase + 2 * r) : "memory");
+    return static_cast<uint32_t>(v >> 32) == x.epoch ? static_cast<int32_t>(static_cast<uint32_t>(v) & 0x7FFFFFFFu) : -1;
+}
+
 // Called by thread 0 of every CTA of a cooperative step once the CTA has finished.
 __device__ __forceinline__ void finish_block(const StepExtra &x)
 {
@@ -944,24 +1016,17 @@ __device__ __forceinline__ void finish_block(const StepExtra &x)
     __threadfence();
 }
 
-__device__ __forceinline__ bool probe_ready(const uint32_t *f, uint32_t epoch)
-{
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    return v == epoch;
-}
-
-// Copies miss rows of ready requests until none are left: items are tiles of blockDim
-// positions in request order, claimed one at a time, gathered as gather_kernel does. The next
-// item's inputs are loaded before the current item's rows are copied (two row lists), so
-// their latency hides under the copy. Run by the copy CTAs from the start and by every SIEVE
-// CTA once its own step is written back.
+// Copies miss rows of ready requests until none are left: item i is the tile of blockDim
+// positions numbered i % parts of the request in ready-queue slot i / parts; items are claimed
+// one at a time and gathered as gather_kernel does. The next item's inputs are loaded before the
+// current item's rows are copied (two row lists), so their latency hides under the copy. Run by
+// the copy CTAs from the start and by every SIEVE CTA once its own step is written back.
 __device__ void copy_ready_rows(const SieveParams &p, const GatherParams &g, const StepExtra &x, unsigned char *smem)
 {
     __shared__ int s_n[2];
     __shared__ long long s_item;
-    __shared__ int s_state;  // next item probed: 1 ready, 0 not yet, -1 gave up waiting
-    __shared__ int s_late;   // the same after waiting (its own word: s_state may still be read)
+    __shared__ int s_req;   // request of the next item: >= 0 published, -1 not yet, -2 gave up waiting
+    __shared__ int s_late;  // the same after waiting (its own word: s_req may still be read)
     const unsigned tid = threadIdx.x, nt = blockDim.x;
     // row list c: sources at smem + 16*nt*c, destinations 8*nt bytes after them
     auto srcs = [&](int c) { return reinterpret_cast<const uint8_t **>(smem + 16 * nt * c); };
@@ -969,84 +1034,290 @@ __device__ void copy_ready_rows(const SieveParams &p, const GatherParams &g, con
     int32_t num_real = *p.num_real;
     if (num_real > p.max_num_reqs) num_real = p.max_num_reqs;
     const int32_t K = p.top_k, tile = static_cast<int32_t>(nt);
-    const int32_t per_req = (K + tile - 1) / tile;
-    const int64_t items = static_cast<int64_t>(num_real > 0 ? num_real : 0) * per_req;
+    const int32_t parts = (K + tile - 1) / tile;
+    const int64_t items = static_cast<int64_t>(num_real > 0 ? num_real : 0) * parts;
     bool inited = false;  // meaningful in thread 0 only
-    auto range = [&](int64_t it, int64_t *lo, int64_t *hi, int32_t *r) {
-        *r = static_cast<int32_t>(it / per_req);
-        *lo = static_cast<int64_t>(*r) * K + (it % per_req) * tile;
-        const int64_t end = static_cast<int64_t>(*r + 1) * K;
-        *hi = *lo + tile < end ? *lo + tile : end;
+    // a published slot value v = (pw << 8) | request; a request outside [0, num_real) is
+    // treated as never published
+    auto checked = [&](int32_t v) { return v >= 0 && (v & 0xFF) < num_real ? v : -2; };
+    // positions of item `it` still to copy: its tile minus the rows below pw, copied already
+    auto range = [&](int64_t it, int32_t v, int64_t *lo, int64_t *hi) {
+        const int32_t r = v & 0xFF, pw = v >> 8;
+        const int64_t first = static_cast<int64_t>(r) * K;
+        const int64_t a = first + (it % parts) * tile, b = first + (pw < K ? pw : K);
+        *lo = a > b ? a : b;
+        const int64_t end = first + K;
+        *hi = a + tile < end ? a + tile : end;
     };
     if (tid == 0) {
         s_n[0] = s_n[1] = 0;
         const int64_t it = claim_item(x, &inited);
         s_item = it;
-        s_state = 0;
-        if (it >= 0 && it < items) s_state = wait_ready(x.flags + it / per_req, x.epoch) ? 1 : -1;
+        s_req = it >= 0 && it < items ? checked(queue_wait(x, it / parts)) : -2;
     }
     __syncthreads();
     int64_t cur = s_item;
     if (cur < 0 || cur >= items) return;
     {
-        int64_t lo, hi;
-        int32_t r;
-        range(cur, &lo, &hi, &r);
+        const int32_t r = s_req;
+        int64_t lo = 0, hi = 0;
+        if (r >= 0) range(cur, r, &lo, &hi);
         const uint8_t *src = nullptr;
         uint8_t *dst = nullptr;
-        const bool ok = s_state == 1 && lo + tid < hi && gather_position<true>(g, lo + tid, &src, &dst);
+        const bool ok = r >= 0 && lo + tid < hi && gather_position<true>(g, lo + tid, &src, &dst);
         list_append(ok, src, dst, srcs(0), dsts(0), &s_n[0]);
-        if (tid == 0 && s_state != 1) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
+        if (tid == 0 && r < 0) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
     }
     __syncthreads();
     for (int c = 0;; c ^= 1) {
         if (tid == 0) {
             const int64_t it = claim_item(x, &inited);
             s_item = it;
-            s_state = it >= 0 && it < items && probe_ready(x.flags + it / per_req, x.epoch) ? 1 : 0;
+            s_req = it >= 0 && it < items ? queue_probe(x, it / parts) : -2;
+            if (s_req >= 0 && (s_req & 0xFF) >= num_real) s_req = -2;
         }
         __syncthreads();
         const int64_t nxt = s_item;
         const bool valid = nxt >= 0 && nxt < items;
-        int state = s_state;
+        int32_t r = s_req;
         int64_t lo = 0, hi = 0;
-        int32_t r = 0;
-        if (valid) range(nxt, &lo, &hi, &r);
+        if (r >= 0) range(nxt, r, &lo, &hi);
         const int64_t pos = lo + tid;
         int8_t miss = 0;
         int32_t t = -1, slot = -1;
         int64_t req = -1, base = 0;
-        if (state == 1 && pos < hi) {  // issued now, consumed after the copy below
+        if (r >= 0 && pos < hi) {  // issued now, consumed after the copy below
             miss = __ldcg(g.is_miss + pos);
             t = g.topk[pos];
             slot = __ldcg(g.slots + pos);
-            req = g.req_pool[r];
-            base = g.host_base[r];
+            req = g.req_pool[r & 0xFF];
+            base = g.host_base[r & 0xFF];
         }
         cta_copy_rows<uint4, kCoopUnroll>(srcs(c), dsts(c), s_n[c], g.row_bytes, x.magic);
         if (valid) {
-            if (state != 1) {
-                if (tid == 0) s_late = wait_ready(x.flags + r, x.epoch) ? 1 : -1;
+            if (r < 0) {
+                if (tid == 0) s_late = checked(queue_wait(x, nxt / parts));
                 __syncthreads();
-                state = s_late;
-                if (state == 1 && pos < hi) {
-                    miss = __ldcg(g.is_miss + pos);
-                    t = g.topk[pos];
-                    slot = __ldcg(g.slots + pos);
-                    req = g.req_pool[r];
-                    base = g.host_base[r];
+                r = s_late;
+                if (r >= 0) {
+                    range(nxt, r, &lo, &hi);
+                    if (lo + tid < hi) {
+                        miss = __ldcg(g.is_miss + lo + tid);
+                        t = g.topk[lo + tid];
+                        slot = __ldcg(g.slots + lo + tid);
+                        req = g.req_pool[r & 0xFF];
+                        base = g.host_base[r & 0xFF];
+                    }
                 }
-                if (tid == 0 && state != 1) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
+                if (tid == 0 && r < 0) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
             }
             const uint8_t *src = nullptr;
             uint8_t *dst = nullptr;
-            const bool ok = state == 1 && pos < hi && gather_eval(g, pos, miss, t, slot, req, base, &src, &dst);
+            const bool ok = r >= 0 && lo + tid < hi && gather_eval(g, lo + tid, miss, t, slot, req, base, &src, &dst);
             list_append(ok, src, dst, srcs(c ^ 1), dsts(c ^ 1), &s_n[c ^ 1]);
         }
         __syncthreads();
         if (!valid) break;
         if (tid == 0) s_n[c] = 0;
     }
+}
+
+// ---- cooperative step: the walk helpers ----
+// While warp 0 walks, the warps of the other three SM sub-partitions (warp % 4 != 0: 12 of
+// 16) copy rows; the walk warp's own sub-partition keeps its issue slots and memory queue.
+constexpr int kHelpers = (kFastThreads / 32 - kFastThreads / 128) * 32;
+
+__device__ __forceinline__ bool is_walk_helper(int tid) { return (tid >> 5) % 4 != 0; }
+
+// This helper's index among the helper threads.
+__device__ __forceinline__ int helper_index(int tid)
+{
+    const int w = tid >> 5;
+    return (w - 1 - w / 4) * 32 + (tid & 31);
+}
+
+__device__ __forceinline__ bool helper_sync_or(bool v)
+{
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 2, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+                 : "=r"(r)
+                 : "r"(static_cast<uint32_t>(v)), "r"(kHelpers)
+                 : "memory");
+    return r != 0;
+}
+
+// Every candidate's table entry is checked first, as phase 3 checks the evicted ones (only
+// candidates are ever evicted), so the walk's decisions hold as it commits them; *verified
+// reports that all passed (phase 3 then skips its check), and if any failed nothing is
+// listed. Then warp 1 lists the misses the walk has numbered, in number order: numbers below
+// prog[0] are final (a miss the walk creates always follows every miss consumed before it),
+// each number's position being that set bit of the miss queue. Entry m of request bid's walk
+// list is {token, (position << 16) | slot}; after each batch the count is published
+// (wl_publish). Listing stops when the walk has ended (prog[1]). Returns (in warp 1) how many
+// numbers were listed: exactly the misses at positions below the position of that number.
+__device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n, const int32_t *tok,
+                             const uint16_t *ht, uint32_t mask, int32_t padded, const int32_t *topk,
+                             const uint32_t *missb, const uint16_t *nslot, const int32_t *prog, int32_t K, int32_t bid,
+                             uint16_t *hpos, int *verified)
+{
+    const unsigned kAll = 0xFFFFFFFFu;
+    const int htid = helper_index(threadIdx.x), lane = threadIdx.x & 31;
+    bool bad = false;
+    for (int32_t i = htid; i < n; i += kHelpers) {
+        const int32_t c = static_cast<int32_t>(reinterpret_cast<const volatile uint32_t *>(cand)[i] & 0xFFFFu);
+        const int32_t t = tok[c];
+        if (t < 0) continue;
+        uint32_t idx = ht_hash(t) & mask;
+        int32_t found = -1;
+        bool ended = false, dup = false;
+        for (uint32_t q = 0; q <= mask; ++q) {
+            const uint16_t e = ht[idx];
+            if (e == kHtEmpty) {
+                ended = true;
+                break;
+            }
+            if (tok_of(tok, e, padded) == t) {
+                if (found >= 0) {
+                    dup = true;
+                    break;
+                }
+                found = static_cast<int32_t>(e) - 1;
+            }
+            idx = (idx + 1) & mask;
+        }
+        if (found != c || dup || !ended) bad = true;
+    }
+    if (helper_sync_or(bad) || htid >= 32) return 0;
+    if (lane == 0) *verified = 1;
+    if (x.wl == nullptr) return 0;
+    const int32_t qwords = (K + 31) >> 5;
+    const volatile int32_t *vprog = prog;
+    uint2 *wl = x.wl + static_cast<int64_t>(bid) * K;
+    int32_t m0 = 0, wb = 0, nb = 0;  // cursor: first word that may hold number m0; misses before it
+    for (uint32_t iter = 0; iter < (1u << 22); ++iter) {
+        int32_t done = 0, gm = 0;
+        if (lane == 0) {
+            done = vprog[1];
+            __threadfence_block();
+            gm = vprog[0];
+        }
+        done = __shfl_sync(kAll, done, 0);
+        gm = __shfl_sync(kAll, gm, 0);
+        if (done) break;
+        const int32_t m1 = min(gm, m0 + kHelpBatch);
+        if (m1 <= m0) {  // nothing new yet
+            __nanosleep(128);
+            continue;
+        }
+        __threadfence_block();
+        bool found = false;
+        for (int32_t w = wb, before = nb; w < qwords;) {  // positions of numbers [m0, m1)
+            const uint32_t W = w + lane < qwords ? reinterpret_cast<const volatile uint32_t *>(missb)[w + lane] : 0u;
+            const int32_t pc = __popc(W);
+            int32_t incl = pc;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int32_t v = __shfl_up_sync(kAll, incl, d);
+                if (lane >= d) incl += v;
+            }
+            const int32_t ex = before + incl - pc;
+            if (ex < m1 && ex + pc > m0) {
+                int32_t num = ex;
+                for (uint32_t b = W; b != 0u && num < m1; b &= b - 1u, ++num)
+                    if (num >= m0) hpos[num - m0] = static_cast<uint16_t>((w + lane) * 32 + __ffs(b) - 1);
+            }
+            const unsigned reach = __ballot_sync(kAll, before + incl >= m1);
+            if (reach != 0u) {  // the word holding number m1 - 1 is where the next batch starts
+                const int lr = __ffs(reach) - 1;
+                nb = __shfl_sync(kAll, ex, lr);
+                wb = w + lr;
+                found = true;
+                break;
+            }
+            before += __shfl_sync(kAll, incl, 31);
+            w += 32;
+        }
+        if (!found) break;  // cannot happen: numbers below prog[0] are set bits
+        __syncwarp();
+        for (int32_t j = lane; j < m1 - m0; j += 32) {
+            const uint32_t pos = hpos[j];
+            wl[m0 + j] = make_uint2(static_cast<uint32_t>(topk[pos]), (pos << 16) | nslot[m0 + j]);
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) wl_publish(x, bid, m1, false);
+        m0 = m1;
+    }
+    return m0;
+}
+
+// Copy CTA cidx of ncopy during the walks: follows the walk lists of requests cidx, cidx +
+// ncopy, ... (lane i of warp 0 polls the i-th; there are at most 32 since ncopy >= 8), copying
+// each list's published entries in order, until every list it follows is final and copied.
+__device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t num_real,
+                                int32_t K, int32_t cidx, int32_t ncopy)
+{
+    __shared__ int32_t s_r, s_t0, s_t1;
+    __shared__ int s_wn;
+    const unsigned kAll = 0xFFFFFFFFu;
+    const unsigned tid = threadIdx.x, nt = blockDim.x;
+    const int lane = tid & 31;
+    const uint8_t **srcl = reinterpret_cast<const uint8_t **>(smem);
+    uint8_t **dstl = reinterpret_cast<uint8_t **>(smem + 8 * nt);
+    const int32_t own = cidx < num_real ? min((num_real - cidx + ncopy - 1) / ncopy, 32) : 0;
+    if (own == 0) return;
+    if (tid == 0) s_wn = 0;
+    int32_t mine = 0;  // warp 0: entries of lane's list copied (issued) so far
+    bool finished = false;
+    for (uint32_t iter = 0; iter < (1u << 22) && !finished; ++iter) {
+        if (tid < 32) {
+            const int32_t r = cidx + lane * ncopy;
+            int32_t avail = 0;
+            bool fin = true;
+            if (lane < own) {
+                const int32_t pv = wl_probe(x, r);
+                const int32_t cnt = pv < 0 ? 0 : (pv >> 1);
+                avail = cnt - mine;
+                fin = pv >= 0 && (pv & 1) != 0 && avail <= 0;
+            }
+            const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
+            const unsigned allfin = __ballot_sync(kAll, fin);
+            if (best > 0) {
+                const int pick = __ffs(__ballot_sync(kAll, avail == best)) - 1;
+                if (lane == pick) {
+                    s_r = r;
+                    s_t0 = mine;
+                    s_t1 = mine + min(best, static_cast<int32_t>(nt));
+                    mine = s_t1;
+                }
+            } else if (lane == 0) {
+                s_r = allfin == kAll ? -2 : -1;
+            }
+        }
+        __syncthreads();
+        const int32_t r = s_r;
+        if (r == -2) {
+            finished = true;
+        } else if (r >= 0) {
+            const int32_t t0 = s_t0, t1 = s_t1;
+            const uint8_t *src = nullptr;
+            uint8_t *dst = nullptr;
+            bool ok = false;
+            if (t0 + static_cast<int32_t>(tid) < t1) {
+                const uint2 e = __ldcg(x.wl + static_cast<int64_t>(r) * K + t0 + tid);
+                const int32_t pos = static_cast<int32_t>(e.y >> 16), slot = static_cast<int32_t>(e.y & 0xFFFFu);
+                ok = gather_eval(g, static_cast<int64_t>(r) * K + pos, 1, static_cast<int32_t>(e.x), slot,
+                                 g.req_pool[r], g.host_base[r], &src, &dst);
+            }
+            list_append(ok, src, dst, srcl, dstl, &s_wn);
+            __syncthreads();
+            cta_copy_rows<uint4, kCoopUnroll>(srcl, dstl, s_wn, g.row_bytes, x.magic);
+        } else {
+            __nanosleep(256);
+        }
+        __syncthreads();
+        if (tid == 0) s_wn = 0;
+    }
+    if (tid == 0 && !finished) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
 }
 
 // kMode 0: SIEVE step only (hisp_sieve_update). 1: plus a copy warp that moves the miss rows
@@ -1062,18 +1333,21 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ uint32_t s_epoch;
     StepExtra x = x0;
-    if (kMode == 2) {
-        if (threadIdx.x == 0) {
-            s_epoch = *reinterpret_cast<volatile const uint32_t *>(x0.flags + kEpochWord) + 1u;
-            if (blockIdx.x == 0) {
-                x.epoch = s_epoch;
-                init_claims(x);
-            }
-        }
+    // The step's epoch (one more than the last finished step's): loaded at entry. A copy CTA
+    // needs it at once; a SIEVE CTA takes it once its first loads are in flight, and its other
+    // threads after the staging barrier.
+    uint32_t epoch_raw = 0;
+    if (kMode == 2 && threadIdx.x == 0) epoch_raw = *reinterpret_cast<volatile const uint32_t *>(x0.flags + kEpochWord);
+    if (kMode == 2 && static_cast<int32_t>(blockIdx.x) >= p.max_num_reqs) {  // a copy CTA
+        if (threadIdx.x == 0) s_epoch = epoch_raw + 1u;
         __syncthreads();
         x.epoch = s_epoch;
-    }
-    if (kMode == 2 && static_cast<int32_t>(blockIdx.x) >= p.max_num_reqs) {  // a copy CTA
+        if (x.wl != nullptr) {  // rows of the misses the walks number, while they walk
+            const int32_t nr = min(*p.num_real, p.max_num_reqs);
+            copy_walk_lists(g, x, smem, nr, p.top_k, static_cast<int32_t>(blockIdx.x) - p.max_num_reqs,
+                            static_cast<int32_t>(gridDim.x) - p.max_num_reqs);
+            __syncthreads();
+        }
         copy_ready_rows(p, g, x, smem);
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -1088,6 +1362,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __shared__ bool s_dirty;
     __shared__ int32_t s_warp[32];
     __shared__ int32_t s_ncand, s_last, s_nkeys, s_ndel, s_n0, s_nvis;
+    __shared__ int s_qinit;     // cooperative step: kClaimInit showed this epoch
+    __shared__ int32_t s_qslot;  // cooperative step: the ready-queue slot taken for the fallback
+    __shared__ int32_t s_prog[2];  // cooperative step: misses the walk has consumed; walk ended
+    __shared__ int32_t s_hm, s_pwalk;  // walk list: numbers listed; positions below s_pwalk listed
+    __shared__ int s_hver;             // every candidate's table entry checked (phase 3 need not)
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -1097,12 +1376,21 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     int32_t num_real = *p.num_real;
     if (num_real > p.max_num_reqs) num_real = p.max_num_reqs;  // hisp_sieve_update.cpp:31-34
     const int64_t req = bid < num_real ? p.req_pool[bid] : -1;
+    if (kMode == 2 && tid == 0) {
+        s_epoch = epoch_raw + 1u;
+        x.epoch = s_epoch;
+        if (bid == 0) init_claims(x);
+    }
     if (bid >= num_real || req < 0 || req >= p.pool_size) {  // :72-88
         fill_dummy(g_slots, g_miss, K);
         if (kMode != 0) {  // no rows to copy (all miss flags 0); the CTA still completes the status
             __syncthreads();
             if (kMode == 2) {
-                if (tid == 0) raise_ready(x, bid);
+                x.epoch = s_epoch;
+                if (tid == 0 && bid < num_real) {
+                    wl_publish(x, bid, 0, true);
+                    queue_claim_publish(x, bid);
+                }
                 copy_ready_rows(p, g, x, smem);
                 __syncthreads();
             }
@@ -1158,9 +1446,16 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         s_hand = hand;
         s_flag = 0;
         s_any_miss = 0;
+        s_qinit = 0;
+        s_qslot = -1;
+        s_prog[0] = s_prog[1] = 0;
+        s_hm = 0;
+        s_pwalk = 0;
+        s_hver = 0;
     }
     cp_async_wait_all();
     __syncthreads();
+    if (kMode == 2) x.epoch = s_epoch;
 
     // ---- phase 1: classify and probe every position against the step-initial table ----
     for (int32_t k = tid; k < K; k += nt) {
@@ -1227,7 +1522,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
     if (!s_flag) build_candidates(s_vini, s_tf, s_cand, s_wofs, dbs, &s_ncand, s_warp);
     __syncthreads();
-    if (!s_flag && tid < 32) {
+    // Every thread reads the flag before the walk can set it; a barrier separates the two, so
+    // all 15 helper warps take the same branch (their named barrier counts all of them).
+    const bool walk_step = !s_flag;
+    if (kMode == 2) __syncthreads();
+    if (walk_step && tid < 32) {
         const int32_t n = s_ncand;
         const int32_t h0 = s_hand;
         // first candidate at or after the hand, in slot order
@@ -1235,7 +1534,13 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
                      __popc(~s_vini[h0 >> 5] & ((1u << (h0 & 31)) - 1u));
         if (n0 >= n) n0 = 0;
         int32_t last = -1, nvis = 0;
-        const bool ok = walk_candidates(s_cand, n, n0, s_evt, s_missb, K, &last, &nvis);
+        const bool ok = walk_candidates(s_cand, n, n0, s_evt, s_missb, K, &last, &nvis,
+                                        kMode == 2 ? reinterpret_cast<uint16_t *>(smem + L.nslot) : nullptr,
+                                        kMode == 2 ? s_prog : nullptr);
+        if (kMode == 2 && tid == 0) {  // the walk has ended: the helpers stop after their batch
+            __threadfence_block();
+            reinterpret_cast<volatile int32_t *>(s_prog)[1] = 1;
+        }
         if (tid == 0) {
             if (!ok) s_flag = 1;
             s_last = last;
@@ -1243,10 +1548,10 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             s_n0 = n0;
             s_nvis = nvis;
         }
-    } else if (kMode == 2 && !s_flag) {
-        // Cooperative step: while one warp walks, the others start pulling this request's
-        // initial miss rows (first lookups of non-resident tokens) into L2, so that the copy
-        // CTAs read them from L2 once the slots are known.
+    } else if (kMode == 2 && walk_step) {
+        // Cooperative step: while one warp walks, the others first pull this request's initial
+        // miss rows (first lookups of non-resident tokens) into L2, then list the misses the
+        // walk has numbered (help_walk) for the copy CTAs, which copy them during the walk.
         const int64_t hb = g.host_base[bid];
         for (int32_t k = tid - 32; k < K; k += nt - 32) {
             if (s_cls[k] != kClsNew || s_aux[k] != k) continue;
@@ -1257,12 +1562,27 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             if (seg == nullptr || seg_row >= g.plsr) continue;
             prefetch_l2(seg + (g.layer_offset_rows + seg_row) * static_cast<uint64_t>(g.row_bytes), g.row_bytes);
         }
+        if (tid == 32) s_qinit = wait_ready(x.flags + kClaimInit, x.epoch) ? 1 : 0;  // off the walk's path
+        if (is_walk_helper(tid)) {
+            const int32_t hm = help_walk(x, s_cand, s_ncand, s_tok, s_ht, mask, padded, s_topk, s_missb,
+                                         reinterpret_cast<const uint16_t *>(smem + L.nslot), s_prog, K, bid,
+                                         reinterpret_cast<uint16_t *>(smem + L.hpos), &s_hver);
+            if (tid == 32) s_hm = hm;
+        }
     }
     __syncthreads();
+    // Cooperative step: the ready-queue slot is taken as the walk ends, so slots follow the
+    // order in which requests become ready; the atomic's latency hides under phases 2b-3.
+    int32_t qk = -1;
+    if (kMode == 2 && tid == 0 && !s_flag && s_qinit) qk = queue_claim(x);
     if (!s_flag)
         resolve_miss_numbers(s_missb, K, reinterpret_cast<uint16_t *>(smem + L.posl), s_evt, s_os, s_om, s_cand,
                              s_ncand, s_n0, s_nvis, dbs, s_warp);
     __syncthreads();
+    if (kMode == 2 && tid == 0 && !s_flag) {  // the walk list holds every miss below this position
+        const int32_t gm = s_prog[0];
+        s_pwalk = s_hm < gm ? static_cast<int32_t>(reinterpret_cast<const uint16_t *>(smem + L.posl)[s_hm]) : K;
+    }
     if (!s_flag && s_last >= 0) {
         passed_bits(s_vini, s_vfin, s_tf, s_evt, s_cand, s_wofs, s_ncand, dbs, s_hand, s_last);
         if (tid == 0) s_hand = s_last + 1 == dbs ? 0 : s_last + 1;
@@ -1271,7 +1591,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
 
     // ---- phase 3: table check for the evicted tokens; outputs of the hits ----
     if (!s_flag) {
-        for (int32_t c = tid; c < dbs; c += nt) {
+        for (int32_t c = s_hver ? dbs : tid; c < dbs; c += nt) {  // s_hver: checked during the walk
             if (s_evt[c] == kNone16) continue;
             const int32_t t = s_tok[c];
             if (t < 0) continue;
@@ -1344,7 +1664,13 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         coop_copy(g_slots, s_os, 4ull * K);
         coop_copy(g_miss, s_om, static_cast<size_t>(K));
         __syncthreads();
-        if (tid == 0) raise_ready(x, bid);
+        if (tid == 0) {
+            wl_publish(x, bid, s_hm, true);
+            if (qk >= 0) queue_publish(x, qk, bid, s_pwalk);
+            else queue_claim_publish(x, bid, s_pwalk);
+        }
+    } else if (kMode == 2 && tid == 0) {
+        s_qslot = qk;  // published after the sequential path
     }
 
     // ---- phase 4: delete the evicted tokens from the table, re-packing each probe run ----
@@ -1526,7 +1852,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     if (kFused) __syncthreads();  // meets the copy warp
     if (kMode == 2) {  // a fallback raised later rewrote the published outputs with equal values
         __syncthreads();
-        if (tid == 0 && !raised) raise_ready(x, bid);
+        if (tid == 0 && !raised) {
+            wl_publish(x, bid, s_hm, true);  // the listed prefix is exact; every row is copied again
+            if (s_qslot >= 0) queue_publish(x, s_qslot, bid, 0);
+            else queue_claim_publish(x, bid);
+        }
         copy_ready_rows(p, g, x, smem);
         __syncthreads();
         if (tid == 0) {
@@ -1649,7 +1979,7 @@ cudaError_t prepare_sieve_coop(const SieveParams &p)
     return coop_residency(coop_smem(p), &resident);
 }
 
-cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, cudaStream_t s,
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl, cudaStream_t s,
                               bool *launched)
 {
     *launched = false;
@@ -1662,6 +1992,7 @@ cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint3
     if (resident - p.max_num_reqs < 8) return cudaSuccess;
     StepExtra x{};
     x.flags = flags;
+    x.wl = wl;
     const uint32_t cpr = g.row_bytes / 16;  // helpers copy 16-byte chunks (host-checked)
     x.magic = (cpr > 0 && cpr < 65536 && static_cast<uint64_t>(kFastThreads) * cpr < 65536)
                   ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;
