@@ -1242,10 +1242,13 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
             const uint32_t pos = hpos[j];
             wl[m0 + j] = make_uint2(static_cast<uint32_t>(topk[pos]), (pos << 16) | nslot[m0 + j]);
         }
+        m0 = m1;
+        // If the walk has ended meanwhile, the final publish (after the CTA's barrier and fence)
+        // covers this batch: skip the fence, which the CTA would wait for.
+        if (__shfl_sync(kAll, lane == 0 ? vprog[1] : 0, 0) != 0) break;
         __threadfence();
         __syncwarp();
         if (lane == 0) wl_publish(x, bid, m1, false);
-        m0 = m1;
     }
     return m0;
 }
@@ -1665,6 +1668,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         coop_copy(g_miss, s_om, static_cast<size_t>(K));
         __syncthreads();
         if (tid == 0) {
+            __threadfence();  // the walk list's last entries and the outputs above
             wl_publish(x, bid, s_hm, true);
             if (qk >= 0) queue_publish(x, qk, bid, s_pwalk);
             else queue_claim_publish(x, bid, s_pwalk);
@@ -1853,6 +1857,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     if (kMode == 2) {  // a fallback raised later rewrote the published outputs with equal values
         __syncthreads();
         if (tid == 0 && !raised) {
+            __threadfence();
             wl_publish(x, bid, s_hm, true);  // the listed prefix is exact; every row is copied again
             if (s_qslot >= 0) queue_publish(x, s_qslot, bid, 0);
             else queue_claim_publish(x, bid);

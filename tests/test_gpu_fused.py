@@ -30,7 +30,7 @@ class Side:
 def run_twins(seed=0, R=8, K=512, ctx=4096, dbs=1024, N=1, S=1, injective=False, row_bytes=1152, steps=3,
               miss=0.2, block_dim=1, num_real=None, bad_req=False, ext=16, invalid=0.01, dup=0.01, corrupt=False,
               segs_on_host=False, null_seg=None, plsr_cut=None, stride=True, layers=2, layer=1, path="coop",
-              expect=None):
+              expect=None, racy_hot=False):
     import torch
     mod = kv()
     rng = np.random.default_rng(seed)
@@ -114,6 +114,11 @@ def run_twins(seed=0, R=8, K=512, ctx=4096, dbs=1024, N=1, S=1, injective=False,
         assert (ea & ~0xFF) == (eb & ~0xFF) and (ea == eb or (ea & ~0xFF) == 0x10200), (hex(ea), hex(eb))
         assert ra == [ea] * len(ra) and rb == [eb] * len(rb)
         total_err.append(eb)
+        if racy_hot:  # single step, N = 1: see racy_hot_ok
+            for side in (a, b):
+                racy_hot_ok(host(side.hot), hot_h, topk, req_pool, host_base, exp_slots, exp_miss, segs_h[0],
+                            layer * plsr, plsr, row_bytes, dbs)
+            continue
         np.testing.assert_array_equal(host(b.hot), host(a.hot))
         if null_seg is None and plsr_cut is None:
             oracle.gather_all(segs_h, layer * plsr, row_bytes, topk, req_pool, host_base, exp_slots, exp_miss, nr,
@@ -124,6 +129,36 @@ def run_twins(seed=0, R=8, K=512, ctx=4096, dbs=1024, N=1, S=1, injective=False,
             mod.segment_free(x)
     del keep
     return total_err
+
+
+def racy_hot_ok(hot, before, topk, req_pool, host_base, slots, miss, seg, layer_off, plsr, rb, dbs):
+    """Hot rows (per-request stride dbs) after one step whose misses outnumber the slots: the sweep
+    wraps and evicts slots filled earlier in the same step, so several miss positions can name one
+    slot. The gather copies every position independently (kvc_gather_rows.cpp:54-76 has no order
+    either), so each 16-byte chunk of such a slot must come from one of those rows; a slot named
+    once holds exactly its row; any other slot is unchanged."""
+    R, K = topk.shape
+    hot = hot.reshape(-1, rb)
+    before = before.reshape(-1, rb)
+    shared = 0
+    for b in range(R):
+        req, base = int(req_pool[b]), int(host_base[b])
+        for sl in range(dbs):
+            pos = [k for k in range(K) if miss[b, k] and slots[b, k] == sl and topk[b, k] >= 0
+                   and base + int(topk[b, k]) < plsr]
+            got = hot[req * dbs + sl]
+            if not pos:
+                np.testing.assert_array_equal(got, before[req * dbs + sl])
+                continue
+            rows = np.stack([seg[(layer_off + base + int(topk[b, k])) * rb:(layer_off + base + int(topk[b, k]) + 1) * rb]
+                             for k in pos])
+            if len(pos) == 1:
+                np.testing.assert_array_equal(got, rows[0])
+                continue
+            shared += 1
+            ok = (rows.reshape(len(pos), -1, 16) == got.reshape(1, -1, 16)).all(axis=2).any(axis=0)
+            assert ok.all(), (b, sl, pos)
+    assert shared > 0  # the case this check exists for did occur
 
 
 PATHS = ["coop", "fused"]  # cooperative copy CTAs; copy warp with bulk copies
@@ -146,6 +181,16 @@ def test_sieve_import_other_paths(path):
 @pytest.mark.parametrize("N,S,injective", [(3, 2, False), (3, 2, True), (1, 0, False)])
 def test_fused_striped_over_nodes(N, S, injective, path):
     assert run_twins(N=N, S=S, injective=injective, block_dim=2, seed=3, path=path) == [0, 0, 0]
+
+
+@pytest.mark.parametrize("dbs", [128, 256])
+def test_coop_walk_that_wraps_falls_back_after_listing(dbs):
+    """More misses than slots: the sweep passes every candidate and would wrap, so the walk
+    gives up after its first pass. The walk list already holds that pass's misses (copy CTAs
+    copy them during the walk); the sequential fallback must agree with them (slots, flags and
+    state equal the C restatement) and every row is copied again. Slots the wrapped sweep
+    names twice are checked chunk by chunk (racy_hot_ok)."""
+    run_twins(R=8, K=512, ctx=4096, dbs=dbs, miss=0.6, steps=1, seed=23 + dbs, path="coop", racy_hot=True)
 
 
 @pytest.mark.parametrize("path", PATHS)
