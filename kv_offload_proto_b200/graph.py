@@ -20,10 +20,13 @@ class StepGraph:
     pool, coord: a DevicePool and an XdsOffloadCoordinator with `set_batch` called.
     hot: per-layer hot-row buffers (hot[l] is passed to layer l's call).
     topk: optional int32 tensor [layers, max_num_reqs, top_k] to read; allocated if None.
+    after_layer: optional callable(layer) whose CUDA work is captured right after that layer's
+    call, e.g. a reduction of the layer's outputs (coord.is_miss, coord.top_k_device_slots),
+    which the next layer overwrites.
     """
 
     def __init__(self, pool, coord, hot: Sequence, layers: Optional[int] = None, *, path: str = "auto",
-                 block_dim: int = 1, hot_req_stride_rows: int = 0, topk=None):
+                 block_dim: int = 1, hot_req_stride_rows: int = 0, topk=None, after_layer=None):
         import torch
         if coord._req_pool_indices is None:
             raise RuntimeError("StepGraph: call coord.set_batch() before capturing")
@@ -45,6 +48,8 @@ class StepGraph:
             for layer in range(self.layers):
                 pool.sieve_and_read(coord, layer, self.topk[layer], hot[layer], s, block_dim,
                                     hot_req_stride_rows=hot_req_stride_rows, path=path, publish=False)
+                if after_layer is not None:
+                    after_layer(layer)
         self.path = k.last_step_path()
 
     def replay(self) -> None:

@@ -30,7 +30,9 @@ def test_step_graph_replay_equals_reference_call_pair(path):
                      torch.full((R,), ctx, dtype=torch.int32, device="cuda"))
         cos.append(co)
         hots.append(torch.zeros((L, R * dbs * RB), dtype=torch.uint8, device="cuda"))
-    graph = StepGraph(pool, cos[1], hots[1], path=path, hot_req_stride_rows=dbs)
+    counts = torch.zeros(L, dtype=torch.int64, device="cuda")  # filled inside the graph (after_layer)
+    graph = StepGraph(pool, cos[1], hots[1], path=path, hot_req_stride_rows=dbs,
+                      after_layer=lambda l: counts[l].copy_(cos[1].is_miss.sum()))
     assert graph.path == ("coop" if path == "auto" else "split")
     torch.cuda.synchronize()
     # capture launched nothing: both sides still start from the admitted state
@@ -39,12 +41,14 @@ def test_step_graph_replay_equals_reference_call_pair(path):
     for step in range(4):
         topk = torch.empty((L, R, K), dtype=torch.int32, device="cuda")
         co = cos[0]
+        ref_counts = []
         for layer in range(L):
             topk[layer] = sample_topk_device(co.device_buffer_tokens[layer, :R], ctx, dbs, K, 0.25, gen)
             co.sieve_update(layer, topk[layer])
             st = pool.batch_read(layer, topk[layer], co._req_pool_indices, co.req_host_base, co.top_k_device_slots,
                                  co.is_miss, co.num_real, hots[0][layer], R, K, 0, 1, hot_req_stride_rows=dbs)
             pool.wait(st)
+            ref_counts.append(int(co.is_miss.sum()))
         graph.topk.copy_(topk)
         graph.replay()
         torch.cuda.synchronize()
@@ -53,6 +57,7 @@ def test_step_graph_replay_equals_reference_call_pair(path):
         for name in ("device_buffer_tokens", "device_buffer_visited", "device_buffer_ht", "sieve_hand"):
             assert torch.equal(getattr(cos[0], name), getattr(cos[1], name)), (step, name)
         assert torch.equal(hots[0], hots[1]), step
+        assert counts.tolist() == ref_counts, step  # per-layer outputs seen by the captured hook
         assert int(cos[1].is_miss.sum()) > 0
     pool.destroy()
 
