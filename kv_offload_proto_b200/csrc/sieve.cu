@@ -609,10 +609,11 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
 
 // 2b': miss numbers -> positions. posl[m] = position of the m-th set bit of the miss queue
 // (all threads), then every evicted slot's number and every visited candidate's arrival
-// number is replaced by its position, and the misses' outputs are written.
+// number is replaced by its position, and the misses' outputs are written. *nmiss: the
+// number of misses.
 __device__ void resolve_miss_numbers(const uint32_t *missb, int32_t K, uint16_t *posl, uint16_t *evt, int32_t *os,
                                      int8_t *om, uint32_t *cand, int32_t n, int32_t n0, int32_t nvis, int32_t dbs,
-                                     int32_t *warp_sums)
+                                     int32_t *warp_sums, int32_t *nmiss)
 {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
     const int32_t nwords = (K + 31) >> 5;
@@ -635,6 +636,7 @@ __device__ void resolve_miss_numbers(const uint32_t *missb, int32_t K, uint16_t 
             if (lane >= d) inc += u;
         }
         if (lane < nw) warp_sums[lane] = inc - v;
+        if (lane == nw - 1) *nmiss = inc;
     }
     __syncthreads();
     int32_t at = warp_sums[wid] + incl - mine;
@@ -894,99 +896,19 @@ __device__ __forceinline__ int warp_append(int32_t *n, bool want)
     return __shfl_sync(0xFFFFFFFFu, at, 0) + __popc(bal & ((1u << lane) - 1u));
 }
 
-// ---- cooperative layer-step: ready words and copy helpers ----
+// ---- cooperative layer-step: walk-list progress words ----
 
-// Waits for a ready word; false after ~2^24 polls (more than a second).
-__device__ __forceinline__ bool wait_ready(const uint32_t *f, uint32_t epoch)
-{
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
-        uint32_t v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-        if (v == epoch) return true;
-        __nanosleep(64);
-    }
-    return false;
-}
-
-// Layout of a launch's block of kCoopBlockWords words. Copy items are claimed with one atomicAdd on
-// kClaimWord; SIEVE CTA 0 zeroes it and kQueueTail at kernel entry before it sets kClaimInit to
-// the epoch (every CTA waits for that once before its first claim, so a count left by an older
-// launch is never used). Requests enter a ready queue in the order their outputs become final:
-// a SIEVE CTA takes the next slot (kQueueTail) and publishes (epoch << 32) | request in it;
-// item i covers part i % parts of the request in slot i / parts, so the copy follows the order
-// in which requests become ready. While a request's walk runs, its walk list (StepExtra::wl)
-// receives one entry per miss number the walk has made final, and kProgBase + 2 r publishes
-// (epoch << 32) | (entries << 1) | final; copy CTAs copy those rows during the walk. The epoch
-// itself lives on the device: every CTA reads kEpochWord at entry and uses its value + 1; the
-// last CTA to finish (kArriveWord) stores that value back. A launch replayed from a CUDA graph
-// therefore gets a new epoch each time without any host work.
-constexpr int kClaimInit = 252, kClaimWord = 253, kArriveWord = 254, kEpochWord = 255, kMaxCoopReqs = 252;
-constexpr int kQueueTail = 256, kQueueBase = 512;  // kMaxCoopReqs 64-bit slots from word 512
-constexpr int kProgBase = 1024;                     // kMaxCoopReqs 64-bit progress words
+// Layout of a launch's block of kCoopBlockWords words. While a request's walk runs, its walk
+// list (StepExtra::wl) receives one entry per miss number the walk has made final, and when the
+// request's outputs are final the rest; word kProgBase + 2 r publishes
+// (epoch << 32) | (entries << 1) | final, and copy CTAs copy the listed rows as they appear.
+// The epoch itself lives on the device: every CTA reads kEpochWord at entry and uses its value
+// + 1; the last CTA to finish (kArriveWord) stores that value back. A launch replayed from a
+// CUDA graph therefore gets a new epoch each time without any host work.
+constexpr int kArriveWord = 254, kEpochWord = 255, kMaxCoopReqs = 252;
+constexpr int kProgBase = 1024;  // kMaxCoopReqs 64-bit progress words
 static_assert(kProgBase + 2 * kMaxCoopReqs <= static_cast<int>(kCoopBlockWords), "block layout");
 constexpr int kCoopUnroll = 12;  // 16-byte loads in flight per thread of a copy CTA
-
-__device__ __forceinline__ void init_claims(const StepExtra &x)
-{
-    *reinterpret_cast<volatile uint32_t *>(x.flags + kClaimWord) = 0u;
-    *reinterpret_cast<volatile uint32_t *>(x.flags + kQueueTail) = 0u;
-    __threadfence();
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(x.flags + kClaimInit), "r"(x.epoch) : "memory");
-}
-
-// The next item index, or -1 if the claim counter was never initialised (not expected).
-__device__ __forceinline__ int64_t claim_item(const StepExtra &x, bool *inited)
-{
-    if (!*inited) {
-        if (!wait_ready(x.flags + kClaimInit, x.epoch)) return -1;
-        *inited = true;
-    }
-    return static_cast<int64_t>(atomicAdd(x.flags + kClaimWord, 1u));
-}
-
-// The next ready-queue slot; the caller has seen kClaimInit hold this epoch.
-__device__ __forceinline__ int32_t queue_claim(const StepExtra &x)
-{
-    return static_cast<int32_t>(atomicAdd(x.flags + kQueueTail, 1u));
-}
-
-// Publishes request r in ready-queue slot k: its slots and miss flags are in global memory
-// (called after a barrier that follows their stores), and its miss rows at positions below
-// pw (0..top_k) are already copied. k < 0: the claim failed; nothing is published and the
-// copy helpers time out on the slot (KVOPS_ERR_COPY_TIMEOUT).
-__device__ __forceinline__ void queue_publish(const StepExtra &x, int32_t k, int32_t r, int32_t pw)
-{
-    if (k < 0 || k >= kMaxCoopReqs) return;
-    __threadfence();
-    const uint64_t v = (static_cast<uint64_t>(x.epoch) << 32) | (static_cast<uint32_t>(pw) << 8) |
-                       static_cast<uint32_t>(r);
-    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(x.flags + kQueueBase + 2 * k), "l"(v) : "memory");
-}
-
-// Claims a slot (waiting for kClaimInit first) and publishes request r in it (pw as above).
-__device__ __forceinline__ void queue_claim_publish(const StepExtra &x, int32_t r, int32_t pw = 0)
-{
-    queue_publish(x, wait_ready(x.flags + kClaimInit, x.epoch) ? queue_claim(x) : -1, r, pw);
-}
-
-// Ready-queue slot k for this epoch: (pw << 8) | request, or -1 while it is not published.
-__device__ __forceinline__ int32_t queue_probe(const StepExtra &x, int64_t k)
-{
-    uint64_t v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(x.flags + kQueueBase + 2 * k) : "memory");
-    return static_cast<uint32_t>(v >> 32) == x.epoch ? static_cast<int32_t>(static_cast<uint32_t>(v) & 0x7FFFFFFFu) : -1;
-}
-
-// Waits for ready-queue slot k; -1 after ~2^24 polls (more than a second).
-__device__ __forceinline__ int32_t queue_wait(const StepExtra &x, int64_t k)
-{
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
-        const int32_t r = queue_probe(x, k);
-        if (r >= 0) return r;
-        __nanosleep(64);
-    }
-    return -1;
-}
 
 // Publishes that request r's walk list holds `entries` entries (final: no more will come).
 // The caller's entry stores are fenced (gpu scope) before this.
@@ -1016,112 +938,6 @@ __device__ __forceinline__ void finish_block(const StepExtra &x)
     __threadfence();
 }
 
-// Copies miss rows of ready requests until none are left: item i is the tile of blockDim
-// positions numbered i % parts of the request in ready-queue slot i / parts; items are claimed
-// one at a time and gathered as gather_kernel does. The next item's inputs are loaded before the
-// current item's rows are copied (two row lists), so their latency hides under the copy. Run by
-// the copy CTAs from the start and by every SIEVE CTA once its own step is written back.
-__device__ void copy_ready_rows(const SieveParams &p, const GatherParams &g, const StepExtra &x, unsigned char *smem)
-{
-    __shared__ int s_n[2];
-    __shared__ long long s_item;
-    __shared__ int s_req;   // request of the next item: >= 0 published, -1 not yet, -2 gave up waiting
-    __shared__ int s_late;  // the same after waiting (its own word: s_req may still be read)
-    const unsigned tid = threadIdx.x, nt = blockDim.x;
-    // row list c: sources at smem + 16*nt*c, destinations 8*nt bytes after them
-    auto srcs = [&](int c) { return reinterpret_cast<const uint8_t **>(smem + 16 * nt * c); };
-    auto dsts = [&](int c) { return reinterpret_cast<uint8_t **>(smem + 16 * nt * c + 8 * nt); };
-    int32_t num_real = *p.num_real;
-    if (num_real > p.max_num_reqs) num_real = p.max_num_reqs;
-    const int32_t K = p.top_k, tile = static_cast<int32_t>(nt);
-    const int32_t parts = (K + tile - 1) / tile;
-    const int64_t items = static_cast<int64_t>(num_real > 0 ? num_real : 0) * parts;
-    bool inited = false;  // meaningful in thread 0 only
-    // a published slot value v = (pw << 8) | request; a request outside [0, num_real) is
-    // treated as never published
-    auto checked = [&](int32_t v) { return v >= 0 && (v & 0xFF) < num_real ? v : -2; };
-    // positions of item `it` still to copy: its tile minus the rows below pw, copied already
-    auto range = [&](int64_t it, int32_t v, int64_t *lo, int64_t *hi) {
-        const int32_t r = v & 0xFF, pw = v >> 8;
-        const int64_t first = static_cast<int64_t>(r) * K;
-        const int64_t a = first + (it % parts) * tile, b = first + (pw < K ? pw : K);
-        *lo = a > b ? a : b;
-        const int64_t end = first + K;
-        *hi = a + tile < end ? a + tile : end;
-    };
-    if (tid == 0) {
-        s_n[0] = s_n[1] = 0;
-        const int64_t it = claim_item(x, &inited);
-        s_item = it;
-        s_req = it >= 0 && it < items ? checked(queue_wait(x, it / parts)) : -2;
-    }
-    __syncthreads();
-    int64_t cur = s_item;
-    if (cur < 0 || cur >= items) return;
-    {
-        const int32_t r = s_req;
-        int64_t lo = 0, hi = 0;
-        if (r >= 0) range(cur, r, &lo, &hi);
-        const uint8_t *src = nullptr;
-        uint8_t *dst = nullptr;
-        const bool ok = r >= 0 && lo + tid < hi && gather_position<true>(g, lo + tid, &src, &dst);
-        list_append(ok, src, dst, srcs(0), dsts(0), &s_n[0]);
-        if (tid == 0 && r < 0) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
-    }
-    __syncthreads();
-    for (int c = 0;; c ^= 1) {
-        if (tid == 0) {
-            const int64_t it = claim_item(x, &inited);
-            s_item = it;
-            s_req = it >= 0 && it < items ? queue_probe(x, it / parts) : -2;
-            if (s_req >= 0 && (s_req & 0xFF) >= num_real) s_req = -2;
-        }
-        __syncthreads();
-        const int64_t nxt = s_item;
-        const bool valid = nxt >= 0 && nxt < items;
-        int32_t r = s_req;
-        int64_t lo = 0, hi = 0;
-        if (r >= 0) range(nxt, r, &lo, &hi);
-        const int64_t pos = lo + tid;
-        int8_t miss = 0;
-        int32_t t = -1, slot = -1;
-        int64_t req = -1, base = 0;
-        if (r >= 0 && pos < hi) {  // issued now, consumed after the copy below
-            miss = __ldcg(g.is_miss + pos);
-            t = g.topk[pos];
-            slot = __ldcg(g.slots + pos);
-            req = g.req_pool[r & 0xFF];
-            base = g.host_base[r & 0xFF];
-        }
-        cta_copy_rows<uint4, kCoopUnroll>(srcs(c), dsts(c), s_n[c], g.row_bytes, x.magic);
-        if (valid) {
-            if (r < 0) {
-                if (tid == 0) s_late = checked(queue_wait(x, nxt / parts));
-                __syncthreads();
-                r = s_late;
-                if (r >= 0) {
-                    range(nxt, r, &lo, &hi);
-                    if (lo + tid < hi) {
-                        miss = __ldcg(g.is_miss + lo + tid);
-                        t = g.topk[lo + tid];
-                        slot = __ldcg(g.slots + lo + tid);
-                        req = g.req_pool[r & 0xFF];
-                        base = g.host_base[r & 0xFF];
-                    }
-                }
-                if (tid == 0 && r < 0) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
-            }
-            const uint8_t *src = nullptr;
-            uint8_t *dst = nullptr;
-            const bool ok = r >= 0 && lo + tid < hi && gather_eval(g, lo + tid, miss, t, slot, req, base, &src, &dst);
-            list_append(ok, src, dst, srcs(c ^ 1), dsts(c ^ 1), &s_n[c ^ 1]);
-        }
-        __syncthreads();
-        if (!valid) break;
-        if (tid == 0) s_n[c] = 0;
-    }
-}
-
 // ---- cooperative step: the walk helpers ----
 // While warp 0 walks, the warps of the other three SM sub-partitions (warp % 4 != 0: 12 of
 // 16) copy rows; the walk warp's own sub-partition keeps its issue slots and memory queue.
@@ -1144,6 +960,46 @@ __device__ __forceinline__ bool helper_sync_or(bool v)
                  : "r"(static_cast<uint32_t>(v)), "r"(kHelpers)
                  : "memory");
     return r != 0;
+}
+
+// Lists every position with om != 0, in position order, as entries 0.. of request bid's walk
+// list; returns the count (all threads; contains barriers).
+__device__ int32_t list_misses_in_order(const StepExtra &x, const int8_t *om, const int32_t *os, const int32_t *topk,
+                                        int32_t K, int32_t bid, int32_t *warp_sums)
+{
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+    const int32_t per = (K + nt - 1) / nt;
+    const int32_t k0 = min(tid * per, K), k1 = min(k0 + per, K);
+    int32_t mine = 0;
+    for (int32_t k = k0; k < k1; ++k) mine += om[k] != 0;
+    int32_t incl = mine;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = nt >> 5;
+        const int32_t v = lane < nw ? warp_sums[lane] : 0;
+        int32_t inc = v;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int32_t u = __shfl_up_sync(0xFFFFFFFFu, inc, d);
+            if (lane >= d) inc += u;
+        }
+        if (lane < nw) warp_sums[lane] = inc - v;
+        if (lane == nw - 1) warp_sums[31] = inc;
+    }
+    __syncthreads();
+    int32_t at = warp_sums[wid] + incl - mine;
+    uint2 *wl = x.wl + static_cast<int64_t>(bid) * K;
+    for (int32_t k = k0; k < k1; ++k)
+        if (om[k] != 0)
+            wl[at++] = make_uint2(static_cast<uint32_t>(topk[k]), (static_cast<uint32_t>(k) << 16) |
+                                                                   static_cast<uint32_t>(os[k]));
+    const int32_t total = warp_sums[31];
+    __syncthreads();
+    return total;
 }
 
 // Every candidate's table entry is checked first, as phase 3 checks the evicted ones (only
@@ -1323,6 +1179,114 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
     if (tid == 0 && !finished) record_error(g.st, KVOPS_ERR_COPY_TIMEOUT);
 }
 
+// Phase 3's outputs of the non-miss positions [t, t + n, ...): a resident token's slot, unless it
+// was evicted before its first lookup (that lookup became a miss; later ones hit its new slot),
+// and a repeated new token hits its first lookup's slot.
+__device__ __forceinline__ void hit_outputs(const uint8_t *cls, const uint16_t *aux, const uint16_t *evt,
+                                            const uint32_t *tf, int32_t *os, int8_t *om, int32_t K, int t, int n)
+{
+    for (int32_t k = t; k < K; k += n) {
+        const uint8_t c = cls[k];
+        if (c == kClsRes) {
+            const int32_t s0 = aux[k];
+            if (evt[s0] != kNone16) {  // evicted before its first lookup, which became a miss
+                const int32_t T = static_cast<int32_t>(tf[s0] & 0xFFFFu);
+                if (k != T) {
+                    os[k] = os[T];
+                    om[k] = 0;
+                }
+            } else {
+                os[k] = s0;
+                om[k] = 0;
+            }
+        } else if (c == kClsNew) {
+            const int32_t k0 = aux[k];
+            if (k != k0) {
+                os[k] = os[k0];
+                om[k] = 0;
+            }
+        }
+    }
+}
+
+// Phase 4 with threads [t, t + n) of the CTA (sync: their barrier). Every miss (posl[0..nkeys),
+// in position order) took exactly one evicted slot (os), so the misses list the deletions: each
+// evicted token's entry is marked deleted and its cell listed in dl (*ndel zero on entry), then
+// the first deleted cell of each probe run leads its re-pack; only listed cells are visited,
+// never the whole table. Touches the table, dl and *ndel only.
+template <typename Sync>
+__device__ void delete_evicted(const uint16_t *posl, int32_t nkeys, const int32_t *os, const uint16_t *evt,
+                               const int32_t *tok, uint16_t *ht, uint32_t mask, int32_t padded, uint16_t *dl,
+                               int32_t *ndel, int t, int n, Sync sync)
+{
+    for (int32_t j0 = 0; j0 < nkeys; j0 += n) {  // mark the evicted entries, listing their cells
+        const int32_t j = j0 + t;
+        bool del = false;
+        uint32_t idx = 0;
+        if (j < nkeys) {
+            const int32_t c = os[posl[j]];
+            if (evt[c] != kNone16 && tok[c] >= 0) {
+                idx = ht_hash(tok[c]) & mask;
+                for (uint32_t q = 0; q <= mask; ++q) {
+                    if (ht[idx] == static_cast<uint16_t>(c + 1)) {
+                        ht[idx] = kDelMark;
+                        del = true;
+                        break;
+                    }
+                    idx = (idx + 1) & mask;
+                }
+            }
+        }
+        const int at = warp_append(ndel, del);
+        if (del) dl[at] = static_cast<uint16_t>(idx);
+    }
+    sync();
+    const int32_t nd = *ndel;
+    for (int32_t j = t; j < nd; j += n) {  // the first deleted cell of each run leads its re-pack
+        const uint32_t i = dl[j];
+        uint32_t q = (i - 1) & mask;
+        bool lead = true;
+        for (uint32_t r = 0; r <= mask; ++r) {
+            const uint16_t e = ht[q];
+            if (e == kHtEmpty) break;
+            if (e == kDelMark || e == kLeadMark) {
+                lead = false;
+                break;
+            }
+            q = (q - 1) & mask;
+        }
+        if (lead) ht[i] = kLeadMark;
+    }
+    sync();
+    for (int32_t j = t; j < nd; j += n) {
+        const uint32_t i = dl[j];
+        if (ht[i] != kLeadMark) continue;
+        // Walk the run from its first deleted cell; every surviving entry moves to the first
+        // empty cell from its home, which is never past its old cell.
+        uint32_t e = i;
+        for (uint32_t r = 0; r <= mask; ++r) {
+            const uint16_t v = ht[e];
+            if (v == kHtEmpty) break;
+            ht[e] = kHtEmpty;
+            if (v != kDelMark && v != kLeadMark) {
+                uint32_t q = ht_hash(tok_of(tok, v, padded)) & mask;
+                for (uint32_t m = 0; m <= mask && ht[q] != kHtEmpty; ++m) q = (q + 1) & mask;
+                ht[q] = v;
+            }
+            e = (e + 1) & mask;
+        }
+    }
+    sync();
+}
+
+constexpr int kHalf = kFastThreads / 2;  // cooperative step: phase 3 and phase 4 side by side
+
+template <int kId>
+__device__ __forceinline__ void half_sync()
+{
+    asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kHalf) : "memory");
+}
+
 // kMode 0: SIEVE step only (hisp_sieve_update). 1: plus a copy warp that moves the miss rows
 // during phases 4-6. 2: cooperative launch with copy helper CTAs after the SIEVE CTAs.
 template <int kMode>
@@ -1345,13 +1309,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         if (threadIdx.x == 0) s_epoch = epoch_raw + 1u;
         __syncthreads();
         x.epoch = s_epoch;
-        if (x.wl != nullptr) {  // rows of the misses the walks number, while they walk
+        if (x.wl != nullptr) {  // the rows of every miss, listed while the walks run and at publish
             const int32_t nr = min(*p.num_real, p.max_num_reqs);
             copy_walk_lists(g, x, smem, nr, p.top_k, static_cast<int32_t>(blockIdx.x) - p.max_num_reqs,
                             static_cast<int32_t>(gridDim.x) - p.max_num_reqs);
-            __syncthreads();
         }
-        copy_ready_rows(p, g, x, smem);
         __syncthreads();
         if (threadIdx.x == 0) {
             arrive_and_publish(g.st);
@@ -1365,10 +1327,8 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __shared__ bool s_dirty;
     __shared__ int32_t s_warp[32];
     __shared__ int32_t s_ncand, s_last, s_nkeys, s_ndel, s_n0, s_nvis;
-    __shared__ int s_qinit;     // cooperative step: kClaimInit showed this epoch
-    __shared__ int32_t s_qslot;  // cooperative step: the ready-queue slot taken for the fallback
     __shared__ int32_t s_prog[2];  // cooperative step: misses the walk has consumed; walk ended
-    __shared__ int32_t s_hm, s_pwalk;  // walk list: numbers listed; positions below s_pwalk listed
+    __shared__ int32_t s_hm;           // walk list: numbers listed during the walk
     __shared__ int s_hver;             // every candidate's table entry checked (phase 3 need not)
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
@@ -1382,7 +1342,6 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     if (kMode == 2 && tid == 0) {
         s_epoch = epoch_raw + 1u;
         x.epoch = s_epoch;
-        if (bid == 0) init_claims(x);
     }
     if (bid >= num_real || req < 0 || req >= p.pool_size) {  // :72-88
         fill_dummy(g_slots, g_miss, K);
@@ -1390,12 +1349,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             __syncthreads();
             if (kMode == 2) {
                 x.epoch = s_epoch;
-                if (tid == 0 && bid < num_real) {
-                    wl_publish(x, bid, 0, true);
-                    queue_claim_publish(x, bid);
-                }
-                copy_ready_rows(p, g, x, smem);
-                __syncthreads();
+                if (tid == 0 && bid < num_real) wl_publish(x, bid, 0, true);
             }
             if (tid == 0) {
                 arrive_and_publish(g.st);
@@ -1449,12 +1403,10 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         s_hand = hand;
         s_flag = 0;
         s_any_miss = 0;
-        s_qinit = 0;
-        s_qslot = -1;
         s_prog[0] = s_prog[1] = 0;
         s_hm = 0;
-        s_pwalk = 0;
         s_hver = 0;
+        s_ndel = 0;
     }
     cp_async_wait_all();
     __syncthreads();
@@ -1565,7 +1517,6 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             if (seg == nullptr || seg_row >= g.plsr) continue;
             prefetch_l2(seg + (g.layer_offset_rows + seg_row) * static_cast<uint64_t>(g.row_bytes), g.row_bytes);
         }
-        if (tid == 32) s_qinit = wait_ready(x.flags + kClaimInit, x.epoch) ? 1 : 0;  // off the walk's path
         if (is_walk_helper(tid)) {
             const int32_t hm = help_walk(x, s_cand, s_ncand, s_tok, s_ht, mask, padded, s_topk, s_missb,
                                          reinterpret_cast<const uint16_t *>(smem + L.nslot), s_prog, K, bid,
@@ -1574,18 +1525,10 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         }
     }
     __syncthreads();
-    // Cooperative step: the ready-queue slot is taken as the walk ends, so slots follow the
-    // order in which requests become ready; the atomic's latency hides under phases 2b-3.
-    int32_t qk = -1;
-    if (kMode == 2 && tid == 0 && !s_flag && s_qinit) qk = queue_claim(x);
     if (!s_flag)
         resolve_miss_numbers(s_missb, K, reinterpret_cast<uint16_t *>(smem + L.posl), s_evt, s_os, s_om, s_cand,
-                             s_ncand, s_n0, s_nvis, dbs, s_warp);
+                             s_ncand, s_n0, s_nvis, dbs, s_warp, &s_nkeys);
     __syncthreads();
-    if (kMode == 2 && tid == 0 && !s_flag) {  // the walk list holds every miss below this position
-        const int32_t gm = s_prog[0];
-        s_pwalk = s_hm < gm ? static_cast<int32_t>(reinterpret_cast<const uint16_t *>(smem + L.posl)[s_hm]) : K;
-    }
     if (!s_flag && s_last >= 0) {
         passed_bits(s_vini, s_vfin, s_tf, s_evt, s_cand, s_wofs, s_ncand, dbs, s_hand, s_last);
         if (tid == 0) s_hand = s_last + 1 == dbs ? 0 : s_last + 1;
@@ -1593,7 +1536,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __syncthreads();
 
     // ---- phase 3: table check for the evicted tokens; outputs of the hits ----
-    if (!s_flag) {
+    // Cooperative step with every candidate's entry checked during the walk: the outputs and
+    // their publication (warps 0-7) run beside phase 4's deletions (warps 8-15), which touch
+    // only the table and their own cell list.
+    const bool overlap = kMode == 2 && !s_flag && s_hver && s_any_miss;
+    if (!s_flag && !overlap) {
         for (int32_t c = s_hver ? dbs : tid; c < dbs; c += nt) {  // s_hver: checked during the walk
             if (s_evt[c] == kNone16) continue;
             const int32_t t = s_tok[c];
@@ -1619,28 +1566,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             }
             if (found != c || dup || !ended) s_flag = 1;
         }
-        for (int32_t k = tid; k < K; k += nt) {
-            const uint8_t cls = s_cls[k];
-            if (cls == kClsRes) {
-                const int32_t s0 = s_aux[k];
-                if (s_evt[s0] != kNone16) {  // evicted before its first lookup, which became a miss
-                    const int32_t T = static_cast<int32_t>(s_tf[s0] & 0xFFFFu);
-                    if (k != T) {
-                        s_os[k] = s_os[T];
-                        s_om[k] = 0;
-                    }
-                } else {
-                    s_os[k] = s0;
-                    s_om[k] = 0;
-                }
-            } else if (cls == kClsNew) {
-                const int32_t k0 = s_aux[k];
-                if (k != k0) {
-                    s_os[k] = s_os[k0];
-                    s_om[k] = 0;
-                }
-            }
-        }
+        hit_outputs(s_cls, s_aux, s_evt, s_tf, s_os, s_om, K, tid, nt);
     }
     __syncthreads();
 
@@ -1660,118 +1586,67 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         return;
     }
     const int ntc = kFused ? kFastThreads : nt;  // threads of the compute role
-    // Cooperative step: the outputs are final now (unless the step already fell back), so
-    // publish them for the copy helpers before the table passes.
     const bool raised = kMode == 2 && !s_flag;
-    if (raised) {
-        coop_copy(g_slots, s_os, 4ull * K);
-        coop_copy(g_miss, s_om, static_cast<size_t>(K));
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();  // the walk list's last entries and the outputs above
-            wl_publish(x, bid, s_hm, true);
-            if (qk >= 0) queue_publish(x, qk, bid, s_pwalk);
-            else queue_claim_publish(x, bid, s_pwalk);
+    const bool update_table = !s_flag && s_any_miss;
+    const uint16_t *posl = reinterpret_cast<const uint16_t *>(smem + L.posl);  // miss positions, in order
+    uint16_t *s_dl = reinterpret_cast<uint16_t *>(smem + L.dkey);  // deleted cells (candidate list no longer needed)
+    const int32_t nkeys = s_nkeys;
+    // Cooperative step: the outputs are final now (unless the step already fell back), so they are
+    // stored, the misses not listed during the walk (numbers [s_hm, G)) complete the walk list,
+    // and the list is published as final, before the table passes.
+    auto publish = [&](int t, int n, auto sync) {
+        coop_copy_n(g_slots, s_os, 4ull * K, t, n);
+        coop_copy_n(g_miss, s_om, static_cast<size_t>(K), t, n);
+        const int32_t gm = s_prog[0];
+        if (x.wl != nullptr) {
+            uint2 *wl = x.wl + static_cast<int64_t>(bid) * K;
+            for (int32_t m = s_hm + t; m < gm; m += n) {
+                const uint32_t pos = posl[m];
+                wl[m] = make_uint2(static_cast<uint32_t>(s_topk[pos]), (pos << 16) | static_cast<uint32_t>(s_os[pos]));
+            }
         }
-    } else if (kMode == 2 && tid == 0) {
-        s_qslot = qk;  // published after the sequential path
-    }
+        sync();
+        if (t == 0) {
+            __threadfence();  // the walk list's entries and the outputs above
+            wl_publish(x, bid, x.wl != nullptr ? gm : 0, true);
+        }
+    };
 
     // ---- phase 4: delete the evicted tokens from the table, re-packing each probe run ----
-    // Every miss took exactly one evicted slot (s_os), so the misses list the deletions; the
-    // passes below visit only the listed cells, never the whole table.
-    const bool update_table = !s_flag && s_any_miss;
-    uint16_t *s_keys = reinterpret_cast<uint16_t *>(smem + L.dkey);  // candidate list no longer needed
-    uint16_t *s_dl = s_keys + K;                                      // table cells deleted this step
-    if (update_table) {
-        if (tid == 0) {
-            s_nkeys = 0;
-            s_ndel = 0;
+    if (overlap) {
+        if (tid < kHalf) {
+            hit_outputs(s_cls, s_aux, s_evt, s_tf, s_os, s_om, K, tid, kHalf);
+            half_sync<3>();
+            publish(tid, kHalf, [] { half_sync<3>(); });
+        } else {
+            delete_evicted(posl, nkeys, s_os, s_evt, s_tok, s_ht, mask, padded, s_dl, &s_ndel, tid - kHalf, kHalf,
+                           [] { half_sync<4>(); });
         }
+        __syncthreads();
+    } else {
+        if (raised) publish(tid, nt, [] { __syncthreads(); });
+        if (update_table)
+            delete_evicted(posl, nkeys, s_os, s_evt, s_tok, s_ht, mask, padded, s_dl, &s_ndel, tid, ntc,
+                           [] { compute_sync<kFused>(); });
         compute_sync<kFused>();
-        for (int32_t m0 = 0; m0 < K; m0 += ntc) {  // list the misses (warp-aggregated appends)
-            const int32_t m = m0 + tid;
-            const bool is_key = m < K && ((s_missb[m >> 5] >> (m & 31)) & 1u);
-            const int at = warp_append(&s_nkeys, is_key);
-            if (is_key) {
-                s_keys[at] = static_cast<uint16_t>(m);
-                s_aux[m] = static_cast<uint16_t>(ht_hash(s_topk[m]) & mask);
-                s_cls[m] = kClsPending;
-            }
-        }
-        compute_sync<kFused>();
-        const int32_t nkeys = s_nkeys;
-        for (int32_t j0 = 0; j0 < nkeys; j0 += ntc) {  // mark the evicted entries, listing their cells
-            const int32_t j = j0 + tid;
-            bool del = false;
-            uint32_t idx = 0;
-            if (j < nkeys) {
-                const int32_t c = s_os[s_keys[j]];
-                if (s_evt[c] != kNone16 && s_tok[c] >= 0) {
-                    idx = ht_hash(s_tok[c]) & mask;
-                    for (uint32_t n = 0; n <= mask; ++n) {
-                        if (s_ht[idx] == static_cast<uint16_t>(c + 1)) {
-                            s_ht[idx] = kDelMark;
-                            del = true;
-                            break;
-                        }
-                        idx = (idx + 1) & mask;
-                    }
-                }
-            }
-            const int at = warp_append(&s_ndel, del);
-            if (del) s_dl[at] = static_cast<uint16_t>(idx);
-        }
     }
-    compute_sync<kFused>();
-    const int32_t ndel = update_table ? s_ndel : 0;
-    for (int32_t j = tid; j < ndel; j += ntc) {  // the first deleted cell of each run leads its re-pack
-        const uint32_t i = s_dl[j];
-        uint32_t q = (i - 1) & mask;
-        bool lead = true;
-        for (uint32_t n = 0; n <= mask; ++n) {
-            const uint16_t e = s_ht[q];
-            if (e == kHtEmpty) break;
-            if (e == kDelMark || e == kLeadMark) {
-                lead = false;
-                break;
-            }
-            q = (q - 1) & mask;
-        }
-        if (lead) s_ht[i] = kLeadMark;
-    }
-    compute_sync<kFused>();
-    for (int32_t j = tid; j < ndel; j += ntc) {
-        const uint32_t i = s_dl[j];
-        if (s_ht[i] != kLeadMark) continue;
-        // Walk the run from its first deleted cell; every surviving entry moves to the first
-        // empty cell from its home, which is never past its old cell.
-        uint32_t e = i;
-        for (uint32_t n = 0; n <= mask; ++n) {
-            const uint16_t v = s_ht[e];
-            if (v == kHtEmpty) break;
-            s_ht[e] = kHtEmpty;
-            if (v != kDelMark && v != kLeadMark) {
-                uint32_t q = ht_hash(tok_of(s_tok, v, padded)) & mask;
-                for (uint32_t m = 0; m <= mask && s_ht[q] != kHtEmpty; ++m) q = (q + 1) & mask;
-                s_ht[q] = v;
-            }
-            e = (e + 1) & mask;
-        }
-    }
-    compute_sync<kFused>();
 
     // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
     // One pass per round: a placed key first checks that it still owns its cell (a displaced
     // one moves on), a pending key then tries its current cell. The round's barrier ORs the
     // progress flags; a round without a pending or displaced key leaves the table final.
     if (update_table) {
-        const int32_t nkeys = s_nkeys;
+        for (int32_t j = tid; j < nkeys; j += ntc) {  // every miss starts at its token's home cell
+            const int32_t m = posl[j];
+            s_aux[m] = static_cast<uint16_t>(ht_hash(s_topk[m]) & mask);
+            s_cls[m] = kClsPending;
+        }
+        compute_sync<kFused>();
         const int32_t limit = 4 * p.ht_size + 64;
         for (int32_t round = 0;; ++round) {
             bool ch = false;
             for (int32_t j = tid; j < nkeys; j += ntc) {
-                const int32_t m = s_keys[j];
+                const int32_t m = posl[j];
                 const uint16_t entry = static_cast<uint16_t>(s_os[m] + 1);
                 uint8_t cls = s_cls[m];
                 uint32_t at = s_aux[m];
@@ -1819,9 +1694,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         if (s_any_miss) coop_copy_n(g_ht, s_ht, 2ull * p.ht_size, tid, ntc);
         if (tid == 0) *g_hand = s_hand;
         if (kFused) __syncthreads();  // meets the copy warp
-        if (kMode == 2) {  // the step is written back: help copy, then complete the status
-            __syncthreads();
-            copy_ready_rows(p, g, x, smem);
+        if (kMode == 2) {  // the step is written back: complete the status
             __syncthreads();
             if (tid == 0) {
                 arrive_and_publish(g.st);
@@ -1856,14 +1729,18 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     if (kFused) __syncthreads();  // meets the copy warp
     if (kMode == 2) {  // a fallback raised later rewrote the published outputs with equal values
         __syncthreads();
-        if (tid == 0 && !raised) {
-            __threadfence();
-            wl_publish(x, bid, s_hm, true);  // the listed prefix is exact; every row is copied again
-            if (s_qslot >= 0) queue_publish(x, s_qslot, bid, 0);
-            else queue_claim_publish(x, bid);
+        if (!raised) {
+            // Every miss of the sequential result, in position order, from entry 0: the entries
+            // listed during the walk are an exact prefix of it (the walk is exact up to where it
+            // stopped), so they are rewritten with the same values and the copy CTA, which has
+            // copied some of them already, goes on from where it is.
+            const int32_t n = x.wl != nullptr ? list_misses_in_order(x, s_om, s_os, s_topk, K, bid, s_warp) : 0;
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                wl_publish(x, bid, n, true);
+            }
         }
-        copy_ready_rows(p, g, x, smem);
-        __syncthreads();
         if (tid == 0) {
             arrive_and_publish(g.st);
             finish_block(x);
@@ -1988,6 +1865,7 @@ cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint3
                               bool *launched)
 {
     *launched = false;
+    if (wl == nullptr) return cudaSuccess;  // the copy CTAs move rows only through the walk lists
     if (p.max_num_reqs <= 0 || p.top_k <= 0 || p.max_num_reqs > kMaxCoopReqs) return cudaSuccess;
     if (p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return cudaSuccess;
     const size_t total = coop_smem(p);
