@@ -449,12 +449,13 @@ __device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint3
     int32_t at = warp_sums[wid] + incl - mine;
     for (int32_t w = w0; w < w1; ++w) {
         wofs[w] = static_cast<uint32_t>(at);
-        uint32_t b = bits_of(w);
-        while (b) {
-            const int32_t c = (w << 5) + __ffs(b) - 1;
-            b &= b - 1u;
-            cand[at++] = ((tf[c] & 0xFFFFu) << 16) | static_cast<uint32_t>(c);
-        }
+        at += __popc(bits_of(w));
+    }
+    __syncthreads();
+    for (int32_t c = tid; c < dbs; c += nt) {  // one slot per thread: its word's offset + candidates before it
+        const uint32_t b = bits_of(c >> 5), below = b & ((1u << (c & 31)) - 1u);
+        if ((b >> (c & 31)) & 1u)
+            cand[wofs[c >> 5] + __popc(below)] = ((tf[c] & 0xFFFFu) << 16) | static_cast<uint32_t>(c);
     }
 }
 
