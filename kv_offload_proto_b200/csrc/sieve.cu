@@ -759,15 +759,6 @@ __device__ __forceinline__ void bulk_store(void *dst, uint32_t src_smem, uint32_
         : "memory");
 }
 
-// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned address and size).
-__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes)
-{
-    asm volatile(
-        "{\n\t.reg .u64 g;\n\t"
-        "cvta.to.global.u64 g, %0;\n\t"
-        "cp.async.bulk.prefetch.L2.global [g], %1;\n\t}" ::"l"(src), "r"(bytes)
-        : "memory");
-}
 
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
@@ -1505,19 +1496,8 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             s_nvis = nvis;
         }
     } else if (kMode == 2 && walk_step) {
-        // Cooperative step: while one warp walks, the others first pull this request's initial
-        // miss rows (first lookups of non-resident tokens) into L2, then list the misses the
-        // walk has numbered (help_walk) for the copy CTAs, which copy them during the walk.
-        const int64_t hb = g.host_base[bid];
-        for (int32_t k = tid - 32; k < K; k += nt - 32) {
-            if (s_cls[k] != kClsNew || s_aux[k] != k) continue;
-            const uint32_t row = static_cast<uint32_t>(hb + s_topk[k]);
-            const uint32_t node = node_of(row, g.stripe, g.nodes);
-            const uint32_t seg_row = seg_row_of(row, g.stripe, g.nodes, g.injective != 0);
-            const uint8_t *seg = node < static_cast<uint32_t>(kMaxNodes) ? g.seg[node] : nullptr;
-            if (seg == nullptr || seg_row >= g.plsr) continue;
-            prefetch_l2(seg + (g.layer_offset_rows + seg_row) * static_cast<uint64_t>(g.row_bytes), g.row_bytes);
-        }
+        // Cooperative step: while one warp walks, the others list the misses the walk has numbered
+        // (help_walk) for the copy CTAs, which copy them during the walk.
         if (is_walk_helper(tid)) {
             const int32_t hm = help_walk(x, s_cand, s_ncand, s_tok, s_ht, mask, padded, s_topk, s_missb,
                                          reinterpret_cast<const uint16_t *>(smem + L.nslot), s_prog, K, bid,
