@@ -1108,7 +1108,7 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
                                 int32_t K, int32_t cidx, int32_t ncopy)
 {
     __shared__ int32_t s_r, s_t0, s_t1;
-    __shared__ int s_wn;
+    __shared__ int s_wn, s_last;
     const unsigned kAll = 0xFFFFFFFFu;
     const unsigned tid = threadIdx.x, nt = blockDim.x;
     const int lane = tid & 31;
@@ -1117,21 +1117,22 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
     const int32_t own = cidx < num_real ? min((num_real - cidx + ncopy - 1) / ncopy, 32) : 0;
     if (own == 0) return;
     if (tid == 0) s_wn = 0;
-    int32_t mine = 0;  // warp 0: entries of lane's list copied (issued) so far
+    int32_t mine = 0;              // warp 0: entries of lane's list copied (issued) so far
+    bool done_lane = lane >= own;  // warp 0: lane's list is final and every entry taken
     bool finished = false;
     for (uint32_t iter = 0; iter < (1u << 22) && !finished; ++iter) {
         if (tid < 32) {
             const int32_t r = cidx + lane * ncopy;
-            int32_t avail = 0;
-            bool fin = true;
-            if (lane < own) {
+            int32_t avail = 0, cnt = 0;
+            bool fin = false;
+            if (!done_lane) {
                 const int32_t pv = wl_probe(x, r);
-                const int32_t cnt = pv < 0 ? 0 : (pv >> 1);
+                cnt = pv < 0 ? 0 : (pv >> 1);
+                fin = pv >= 0 && (pv & 1) != 0;
                 avail = cnt - mine;
-                fin = pv >= 0 && (pv & 1) != 0 && avail <= 0;
+                if (fin && avail <= 0) done_lane = true;
             }
             const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
-            const unsigned allfin = __ballot_sync(kAll, fin);
             if (best > 0) {
                 const int pick = __ffs(__ballot_sync(kAll, avail == best)) - 1;
                 if (lane == pick) {
@@ -1139,9 +1140,14 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
                     s_t0 = mine;
                     s_t1 = mine + min(best, static_cast<int32_t>(nt));
                     mine = s_t1;
+                    if (fin && mine >= cnt) done_lane = true;  // this chunk ends a final list
                 }
-            } else if (lane == 0) {
-                s_r = allfin == kAll ? -2 : -1;
+            }
+            // Every list done once this chunk (if any) is copied: no further poll is needed.
+            const bool all_done = __ballot_sync(kAll, done_lane) == kAll;
+            if (lane == 0) {
+                if (best == 0) s_r = all_done ? -2 : -1;
+                s_last = best > 0 && all_done ? 1 : 0;
             }
         }
         __syncthreads();
@@ -1149,6 +1155,7 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
         if (r == -2) {
             finished = true;
         } else if (r >= 0) {
+            if (s_last) finished = true;  // after this copy
             const int32_t t0 = s_t0, t1 = s_t1;
             const uint8_t *src = nullptr;
             uint8_t *dst = nullptr;
