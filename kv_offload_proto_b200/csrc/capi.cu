@@ -343,7 +343,7 @@ bool vec16_ok(const kvb::GatherParams &g)
     return (a & 15) == 0;
 }
 
-// Allocates (once per device) the zeroed ready words of cooperative layer-steps.
+// Allocates (once per device) the zeroed word blocks of cooperative layer-steps.
 int ensure_ready_words(DeviceState *ds)
 {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -352,13 +352,13 @@ int ensure_ready_words(DeviceState *ds)
     cudaError_t e = cudaMalloc(&ds->ready, bytes);
     if (e != cudaSuccess) {
         ds->ready = nullptr;
-        return cuda_fail(e, "cudaMalloc(ready words)");
+        return cuda_fail(e, "cudaMalloc(cooperative step words)");
     }
     e = cudaMemset(ds->ready, 0, bytes);
     if (e != cudaSuccess) {
         cudaFree(ds->ready);
         ds->ready = nullptr;
-        return cuda_fail(e, "cudaMemset(ready words)");
+        return cuda_fail(e, "cudaMemset(cooperative step words)");
     }
     return KVOPS_OK;
 }

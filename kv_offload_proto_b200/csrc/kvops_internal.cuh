@@ -100,7 +100,7 @@ struct ExportParams {
 };
 
 // Extra arguments of the layer-step kernels (sieve.cu).
-// Words of one cooperative layer-step's claim / queue / progress block (layout in sieve.cu).
+// Words of one cooperative layer-step's block: epoch, arrival count, walk-list progress (layout in sieve.cu).
 constexpr uint32_t kCoopBlockWords = 2048;
 
 struct StepExtra {
@@ -160,10 +160,11 @@ cudaError_t launch_export(const ExportParams &p, cudaStream_t s, int sm_count);
 // nothing, when the request's state and the copy ring do not fit shared memory; the caller
 // then runs launch_sieve_update and launch_gather instead.
 cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cudaStream_t s, bool *launched);
-// The same step as one cooperative launch: the SIEVE CTAs publish their slots and miss flags
-// after the hand sweep (ready words in `flags`, a zero-initialised block of 256 words that no
-// other launch uses while this one runs) and every other CTA resident on the GPU copies miss
-// rows of ready requests. *launched = false (nothing launched) when fewer than 8 copy CTAs fit
+// The same step as one cooperative launch: the SIEVE CTAs list each request's misses in its
+// walk list (wl: max_num_reqs x top_k entries) as the hand sweep makes them final, and every
+// other CTA resident on the GPU copies the listed rows (progress words in `flags`, a
+// zero-initialised block of kCoopBlockWords words that no other launch uses while this one
+// runs). *launched = false (nothing launched) when wl is null, fewer than 8 copy CTAs fit
 // beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
 cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl, cudaStream_t s,
                               bool *launched);
