@@ -18,6 +18,17 @@
  * status + my_node*64 + b*8 (b < B), each equal to (1 << 32) | errCode once every
  * row of the launch has landed. That is exactly what EmsPool.wait polls
  * (xds/xds_ems_pool.py:233-241).
+ *
+ * Clearing: every call zeroes the words it will publish before its launch. Words in pinned
+ * host memory (kvops_alloc_status) are zeroed by the host during the call. Words in device
+ * memory are zeroed on the launch stream (cudaMemsetAsync, so the clear is ordered before the
+ * kernel and is captured with it), and must therefore be read in stream order:
+ * kvops_poll_status reads them on the legacy default stream, which is ordered after launches
+ * on the legacy stream and on blocking streams; after a launch on a non-blocking stream, order
+ * the poll yourself (synchronize the stream, or wait on an event recorded after the call).
+ * A slot must not be reused while an earlier launch that publishes into it may still run:
+ * that launch's done word could land after the clear (the reference's EmsPool cycles 8 x N
+ * slots for the same reason).
  */
 #ifndef KVOPS_B200_H
 #define KVOPS_B200_H
@@ -42,7 +53,7 @@ extern "C" {
 /* Device-side errCode bands (kvops/kernel/kvc_common.h:24). */
 #define KVOPS_ERR_SEG_NULL 0x101u  /* segment base is 0: nothing touched (0x1xx, init band) */
 #define KVOPS_ERR_ROW_BASE 0x200u  /* 0x200 + (index & 0xFF) + (1 << 16): row out of the segment */
-#define KVOPS_ERR_COPY_TIMEOUT 0x102u  /* kvops_sieve_import: a row copy did not complete (not expected) */
+#define KVOPS_ERR_COPY_TIMEOUT 0x102u  /* kvops_sieve_import: a copy CTA stopped waiting for a walk list */
 
 /* Largest node count of one layout (common/kv_layout.h:45, KvLayoutValidate). */
 #define KVOPS_MAX_NODES 64
@@ -100,6 +111,17 @@ typedef struct KvopsRowOpts {
      * SPLIT: the SIEVE kernel, then the gather launched as its programmatic dependent.
      * AUTO: COOP when it fits, else SPLIT. */
     uint32_t step_path;
+    /* Error word (0 = none): the address (device memory, or pinned mapped host memory) of a
+     * uint32 into which every launch of the call stores its first device-side errCode by
+     * compare-and-swap from 0, besides (or, with status == 0, instead of) the status words. A
+     * call captured into a CUDA graph publishes no status words; this word is how its replays
+     * report errors. The caller reads it after the launch and clears it. */
+    uint64_t err_word;
+    /* kvops_sieve_import, COOP path: how many times a copy CTA polls the walk lists before it
+     * stops waiting and reports KVOPS_ERR_COPY_TIMEOUT, leaving rows uncopied (0 = the default,
+     * 2^22 polls with a 256 ns back-off, about one second). */
+    uint32_t copy_wait_polls;
+    uint32_t reserved;
 } KvopsRowOpts;
 
 #define KVOPS_STEP_AUTO 0u
@@ -211,7 +233,9 @@ int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t pad
  * All calls share that array (cleared on `stream` before each launch), so calls whose
  * launches overlap on the GPU race and must not be issued. The first call on a device looks
  * up the array's device address; make it before any stream capture. Launches that would
- * need more scratch than the array holds are rejected with KVOPS_E_INVALID. */
+ * need more scratch than the array holds are rejected with KVOPS_E_INVALID. Like every
+ * other entry point it requires kvops_init (KVOPS_E_NOT_INITED before it), and it clears
+ * the status words as they do (pinned words by the host, device words on `stream`). */
 #define KVOPS_NOALLOC_SCRATCH_BYTES 256
 int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg_bases, uint32_t layer_offset_rows,
                                uint32_t per_layer_seg_rows, uint32_t row_bytes, uint64_t topk_indices,

@@ -108,9 +108,11 @@ bool is_host_memory(uint64_t addr)
 }
 
 // Zeroes the status words a launch will publish, before the launch, so a poller never
-// sees the previous use's done word. Pinned host words are written directly; device
-// words are cleared with a synchronous memset, as the reference does (kvops_ext.cpp:252).
-int reset_status(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim)
+// sees the previous use's done word. Pinned host words are written by the host now. Device
+// words are cleared on the launch stream, ordered before the kernel and captured with it
+// into a CUDA graph (the reference's synchronous memset, kvops_ext.cpp:252, is neither; the
+// header states how such words are then read in stream order).
+int reset_status(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim, cudaStream_t stream)
 {
     if (status == 0) return KVOPS_OK;
     if (is_host_memory(status)) {
@@ -120,24 +122,25 @@ int reset_status(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t b
         return KVOPS_OK;
     }
     for (uint32_t n = node_lo; n < node_hi; ++n) {
-        cudaError_t e = cudaMemset(reinterpret_cast<void *>(status + n * 64ull), 0, block_dim * 8ull);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+        cudaError_t e = cudaMemsetAsync(reinterpret_cast<void *>(status + n * 64ull), 0, block_dim * 8ull, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
     }
     return KVOPS_OK;
 }
 
 int make_status_target(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim, DeviceState *ds,
-                       kvb::StatusTarget *st)
+                       uint64_t err_word, cudaStream_t stream, kvb::StatusTarget *st)
 {
     st->status = reinterpret_cast<uint64_t *>(status);
     st->node_lo = node_lo;
     st->node_hi = node_hi;
     st->block_dim = block_dim;
     st->ticket = nullptr;
+    st->err_word = reinterpret_cast<uint32_t *>(err_word);
     if (status == 0) return KVOPS_OK;
     const uint32_t i = ds->next.fetch_add(1, std::memory_order_relaxed) % ds->ring_size;
     st->ticket = ds->ring + i;
-    return reset_status(status, node_lo, node_hi, block_dim);
+    return reset_status(status, node_lo, node_hi, block_dim, stream);
 }
 
 #define KV_REQUIRE_INIT()                                              \
@@ -166,8 +169,9 @@ int build_gather(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo,
         (topk_indices == 0 || req_pool_indices == 0 || req_host_base == 0 || topk_device_slots == 0 ||
          is_miss == 0 || num_real == 0 || hot_row_base == 0))
         return fail(KVOPS_E_INVALID, w + ": a tensor address is 0");
-    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{0, 0, 0};
+    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{};
     if (o.injective > 1) return fail(KVOPS_E_INVALID, w + ": injective must be 0 or 1");
+    if ((o.err_word & 3) != 0) return fail(KVOPS_E_INVALID, w + ": err_word must be 4-byte aligned");
     DeviceState *ds = nullptr;
     int rc = current_device_state(&ds);
     if (rc != KVOPS_OK) return rc;
@@ -191,10 +195,10 @@ int build_gather(uint32_t node_num, const uint64_t *seg_bases, uint32_t node_lo,
     p.max_num_reqs = max_num_reqs;
     p.injective = o.injective;
     for (uint32_t n = 0; n < node_num; ++n) p.seg[n] = reinterpret_cast<const uint8_t *>(seg_bases[n]);
-    rc = make_status_target(status, node_lo, node_hi, block_dim, ds, &p.st);
+    rc = make_status_target(status, node_lo, node_hi, block_dim, ds, o.err_word, reinterpret_cast<cudaStream_t>(stream),
+                            &p.st);
     if (rc != KVOPS_OK) return rc;
     if (max_num_reqs == 0 || top_k == 0) p.num_real = nullptr;  // nothing to scan: still completes the status
-    (void)stream;
     *out = p;
     *ds_out = ds;
     return KVOPS_OK;
@@ -232,8 +236,9 @@ int export_common(uint64_t seg_base, uint32_t plsr, uint32_t row_bytes, uint32_t
     if (row_bytes == 0) return fail(KVOPS_E_INVALID, "export row_bytes must be > 0");
     if (static_cast<uint64_t>(row_lo) + row_cnt > (1ull << 32))
         return fail(KVOPS_E_INVALID, "export row_lo + row_cnt exceeds the 32-bit row space");
-    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{0, 0, 0};
+    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{};
     if (o.injective > 1) return fail(KVOPS_E_INVALID, "export: injective must be 0 or 1");
+    if ((o.err_word & 3) != 0) return fail(KVOPS_E_INVALID, "export: err_word must be 4-byte aligned");
     DeviceState *ds = nullptr;
     int rc = current_device_state(&ds);
     if (rc != KVOPS_OK) return rc;
@@ -266,7 +271,8 @@ int export_common(uint64_t seg_base, uint32_t plsr, uint32_t row_bytes, uint32_t
         }
     }
     p.units_per_layer = units;
-    rc = make_status_target(status, my_node, my_node + 1, block_dim, ds, &p.st);
+    rc = make_status_target(status, my_node, my_node + 1, block_dim, ds, o.err_word,
+                            reinterpret_cast<cudaStream_t>(stream), &p.st);
     if (rc != KVOPS_OK) return rc;
     if (seg_base == 0 && units > 0) {  // null segment: init-band error, nothing touched
         p.units_per_layer = 0;
@@ -424,6 +430,15 @@ bool bulk_copy_ok(const kvb::GatherParams &g, bool *remote)
 namespace kvb {
 // Lets other translation units of this library report a failure through kvops_last_error().
 int set_last_error(int code, const char *msg) { return fail(code, msg); }
+bool is_inited()
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_inited;
+}
+int clear_status_words(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim, cudaStream_t stream)
+{
+    return reset_status(status, node_lo, node_hi, block_dim, stream);
+}
 }  // namespace kvb
 
 extern "C" {
@@ -683,7 +698,7 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
         rc = next_ready_block(sds, static_cast<size_t>(max_num_reqs) * top_k, &words, &wl);
         if (rc != KVOPS_OK) return rc;
         bool launched = false;
-        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, wl, st, &launched);
+        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, wl, opts ? opts->copy_wait_polls : 0u, st, &launched);
         if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import (cooperative)");
         if (launched) {
             t_last_step_path = KVOPS_STEP_COOP;

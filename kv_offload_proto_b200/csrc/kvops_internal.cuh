@@ -47,6 +47,7 @@ struct StatusTarget {
     uint32_t node_hi;
     uint32_t block_dim;
     Ticket *ticket;        // device memory, zero between launches
+    uint32_t *err_word;    // caller's error word (KvopsRowOpts::err_word), nullptr: none
 };
 
 struct SieveParams {
@@ -110,6 +111,7 @@ struct StepExtra {
     uint32_t epoch;     // cooperative step: set in the kernel from the block (host passes 0)
     uint32_t magic;     // copy helpers: multiply-high constant of cta_copy_rows (0: divide)
     uint2 *wl;          // cooperative step: the launch's walk lists, max_num_reqs x top_k entries
+    uint32_t wait_polls;  // cooperative step: walk-list polls of a copy CTA before it gives up
 };
 
 // Publishes completion: called by thread 0 of every CTA after a __syncthreads() that
@@ -139,14 +141,21 @@ __device__ __forceinline__ void arrive_and_publish(const StatusTarget &st)
 }
 
 // Records the first device-side error of a launch (the reference's early-return
-// errCode, kvc_gather_rows.cpp:78-81); later errors are dropped.
+// errCode, kvc_gather_rows.cpp:78-81) in its ticket (published in the status words) and in
+// the caller's error word; later errors are dropped.
 __device__ __forceinline__ void record_error(const StatusTarget &st, unsigned int code)
 {
     if (st.ticket != nullptr) atomicCAS(&st.ticket->err, 0u, code);
+    if (st.err_word != nullptr) atomicCAS_system(st.err_word, 0u, code);
 }
 
 // Records `msg` as the calling thread's last error (capi.cu) and returns `code`.
 int set_last_error(int code, const char *msg);
+// Whether kvops_init has run (and kvops_close has not since).
+bool is_inited();
+// Zeroes the status words [node_lo, node_hi) x [0, block_dim) at `status` before a launch
+// publishes them: pinned host words by the host now, device words on `stream` (capi.cu).
+int clear_status_words(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim, cudaStream_t stream);
 
 // Kernel launchers (defined next to their kernels).
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int sm_count);
@@ -166,8 +175,9 @@ cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cud
 // zero-initialised block of kCoopBlockWords words that no other launch uses while this one
 // runs). *launched = false (nothing launched) when wl is null, fewer than 8 copy CTAs fit
 // beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
-cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl, cudaStream_t s,
-                              bool *launched);
+// wait_polls: walk-list polls of a copy CTA before it reports KVOPS_ERR_COPY_TIMEOUT (0: 2^22).
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl,
+                              uint32_t wait_polls, cudaStream_t s, bool *launched);
 // Sets up, without launching, what the first cooperative step of this shape would: the
 // kernel's shared-memory limit and the cached residency (so a later call may be captured).
 cudaError_t prepare_sieve_coop(const SieveParams &p);

@@ -22,11 +22,12 @@ void check(int rc)
     if (rc != KVOPS_OK) throw std::runtime_error(kvops_last_error());
 }
 
-KvopsRowOpts row_opts(uint64_t hot_req_stride_rows, bool injective)
+KvopsRowOpts row_opts(uint64_t hot_req_stride_rows, bool injective, uint64_t err_word)
 {
     KvopsRowOpts o{};
     o.hot_req_stride_rows = hot_req_stride_rows;
     o.injective = injective ? 1u : 0u;
+    o.err_word = err_word;
     return o;
 }
 
@@ -58,9 +59,9 @@ void import_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows,
                 uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
                 uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base, uint32_t top_k,
                 uint32_t max_num_reqs, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node, uint64_t status,
-                uint64_t stream, uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective)
+                uint64_t stream, uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective, uint64_t err_word)
 {
-    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective, err_word);
     check(kvops_import_seg_ex(channel, seg_base, layer_offset_rows, per_layer_seg_rows, row_bytes, topk_indices,
                               req_pool_indices, req_host_base, topk_device_slots, is_miss, num_real, hot_row_base,
                               top_k, max_num_reqs, stripe_rows, node_num, my_node, status, stream, block_dim, &o));
@@ -70,9 +71,9 @@ void import_multi(const std::vector<uint64_t> &seg_bases, uint32_t layer_offset_
                   uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
                   uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real, uint64_t hot_row_base,
                   uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint64_t status, uint64_t stream,
-                  uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective)
+                  uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective, uint64_t err_word)
 {
-    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective, err_word);
     check(kvops_import_multi(static_cast<uint32_t>(seg_bases.size()), seg_bases.data(), layer_offset_rows,
                              per_layer_seg_rows, row_bytes, topk_indices, req_pool_indices, req_host_base,
                              topk_device_slots, is_miss, num_real, hot_row_base, top_k, max_num_reqs, stripe_rows,
@@ -86,9 +87,11 @@ void sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq
                   uint32_t max_num_reqs, uint32_t pool_size, const std::vector<uint64_t> &seg_bases,
                   uint32_t layer_offset_rows, uint32_t per_layer_seg_rows, uint32_t row_bytes, uint64_t req_host_base,
                   uint64_t hot_row_base, uint32_t stripe_rows, uint64_t status, uint64_t stream, uint32_t block_dim,
-                  uint64_t hot_req_stride_rows, bool injective, const std::string &path)
+                  uint64_t hot_req_stride_rows, bool injective, const std::string &path, uint64_t err_word,
+                  uint32_t copy_wait_polls)
 {
-    KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    KvopsRowOpts o = row_opts(hot_req_stride_rows, injective, err_word);
+    o.copy_wait_polls = copy_wait_polls;
     if (path == "auto") o.step_path = KVOPS_STEP_AUTO;
     else if (path == "fused") o.step_path = KVOPS_STEP_FUSED;
     else if (path == "split") o.step_path = KVOPS_STEP_SPLIT;
@@ -106,9 +109,10 @@ void export_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows,
                 uint32_t row_bytes, uint64_t topk_indices, uint64_t req_pool_indices, uint64_t req_host_base,
                 uint64_t topk_device_slots, uint64_t export_flags, uint64_t num_real, uint64_t hot_row_base,
                 uint32_t top_k, uint32_t max_num_reqs, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
-                uint64_t status, uint64_t stream, uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective)
+                uint64_t status, uint64_t stream, uint32_t block_dim, uint64_t hot_req_stride_rows, bool injective,
+                uint64_t err_word)
 {
-    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective);
+    const KvopsRowOpts o = row_opts(hot_req_stride_rows, injective, err_word);
     check(kvops_export_seg(channel, seg_base, layer_offset_rows, per_layer_seg_rows, row_bytes, topk_indices,
                            req_pool_indices, req_host_base, topk_device_slots, export_flags, num_real, hot_row_base,
                            top_k, max_num_reqs, stripe_rows, node_num, my_node, status, stream, block_dim, &o));
@@ -117,9 +121,9 @@ void export_seg(uint64_t channel, uint64_t seg_base, uint32_t layer_offset_rows,
 void export_seg_alllayer(uint64_t channel, uint64_t seg_base, uint32_t per_layer_seg_rows, uint32_t row_bytes,
                          uint32_t row_lo, uint32_t row_cnt, uint32_t layer_num, uint64_t src_layer0_base,
                          uint64_t src_layer_stride, uint32_t stripe_rows, uint32_t node_num, uint32_t my_node,
-                         uint64_t status, uint64_t stream, uint32_t block_dim, bool injective)
+                         uint64_t status, uint64_t stream, uint32_t block_dim, bool injective, uint64_t err_word)
 {
-    const KvopsRowOpts o = row_opts(0, injective);
+    const KvopsRowOpts o = row_opts(0, injective, err_word);
     check(kvops_export_seg_alllayer_ex(channel, seg_base, per_layer_seg_rows, row_bytes, row_lo, row_cnt, layer_num,
                                        src_layer0_base, src_layer_stride, stripe_rows, node_num, my_node, status,
                                        stream, block_dim, &o));
@@ -184,25 +188,25 @@ PYBIND11_MODULE(_kvops, m)
           py::arg("req_host_base"), py::arg("topk_device_slots"), py::arg("is_miss"), py::arg("num_real"),
           py::arg("hot_row_base"), py::arg("top_k"), py::arg("max_num_reqs"), py::arg("stripe_rows"),
           py::arg("node_num"), py::arg("my_node"), py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1,
-          py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false);
+          py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false, py::arg("err_word") = 0);
     m.def("import_multi", &import_multi, py::arg("seg_bases"), py::arg("layer_offset_rows"),
           py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("topk_indices"), py::arg("req_pool_indices"),
           py::arg("req_host_base"), py::arg("topk_device_slots"), py::arg("is_miss"), py::arg("num_real"),
           py::arg("hot_row_base"), py::arg("top_k"), py::arg("max_num_reqs"), py::arg("stripe_rows"),
           py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1, py::kw_only(),
-          py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false);
+          py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false, py::arg("err_word") = 0);
     // Single-layer indexed export (kvc_scatter_rows; designed in the reference, not in its module).
     m.def("export_seg", &export_seg, py::arg("channel"), py::arg("seg_base"), py::arg("layer_offset_rows"),
           py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("topk_indices"), py::arg("req_pool_indices"),
           py::arg("req_host_base"), py::arg("topk_device_slots"), py::arg("export_flags"), py::arg("num_real"),
           py::arg("hot_row_base"), py::arg("top_k"), py::arg("max_num_reqs"), py::arg("stripe_rows"),
           py::arg("node_num"), py::arg("my_node"), py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1,
-          py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false);
+          py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false, py::arg("err_word") = 0);
     m.def("export_seg_alllayer", &export_seg_alllayer, py::arg("channel"), py::arg("seg_base"),
           py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("row_lo"), py::arg("row_cnt"),
           py::arg("layer_num"), py::arg("src_layer0_base"), py::arg("src_layer_stride"), py::arg("stripe_rows"),
           py::arg("node_num"), py::arg("my_node"), py::arg("status"), py::arg("stream") = 0, py::arg("block_dim") = 1,
-          py::kw_only(), py::arg("injective") = false);
+          py::kw_only(), py::arg("injective") = false, py::arg("err_word") = 0);
     m.def("sieve_update", &sieve_update, py::arg("topk_indices"), py::arg("req_pool_indices"), py::arg("seq_lens"),
           py::arg("prefill_lens"), py::arg("device_buffer_tokens"), py::arg("device_buffer_visited"),
           py::arg("device_buffer_ht"), py::arg("sieve_hand"), py::arg("topk_device_slots"), py::arg("is_miss"),
@@ -218,7 +222,7 @@ PYBIND11_MODULE(_kvops, m)
           py::arg("layer_offset_rows"), py::arg("per_layer_seg_rows"), py::arg("row_bytes"), py::arg("req_host_base"),
           py::arg("hot_row_base"), py::arg("stripe_rows"), py::arg("status"), py::arg("stream") = 0,
           py::arg("block_dim") = 1, py::kw_only(), py::arg("hot_req_stride_rows") = 0, py::arg("injective") = false,
-          py::arg("path") = "auto");
+          py::arg("path") = "auto", py::arg("err_word") = 0, py::arg("copy_wait_polls") = 0);
     m.def("step_prepare", [](uint32_t top_k, uint32_t dbs, uint32_t padded, uint32_t vis_stride, uint32_t max_num_reqs) {
         check(kvops_step_prepare(top_k, dbs, padded, vis_stride, max_num_reqs));
     }, py::arg("top_k"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"), py::arg("visited_stride_b"),

@@ -56,16 +56,6 @@ int noalloc_scratch(void **out)
     return KVOPS_OK;
 }
 
-bool host_word(uint64_t addr)
-{
-    cudaPointerAttributes a{};
-    if (cudaPointerGetAttributes(&a, reinterpret_cast<void *>(addr)) != cudaSuccess) {
-        cudaGetLastError();
-        return true;
-    }
-    return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeUnregistered;
-}
-
 }  // namespace
 
 extern "C" int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg_bases, uint32_t layer_offset_rows,
@@ -77,6 +67,7 @@ extern "C" int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg
                                           const KvopsRowOpts *opts)
 {
     using kvb::set_last_error;
+    if (!kvb::is_inited()) return set_last_error(KVOPS_E_NOT_INITED, "kvops not inited");
     if (node_num == 0 || node_num > KVOPS_MAX_NODES)
         return set_last_error(KVOPS_E_INVALID, "import node_num must be in [1, 64]");
     if (seg_bases == nullptr) return set_last_error(KVOPS_E_INVALID, "import_multi: seg_bases is NULL");
@@ -87,8 +78,9 @@ extern "C" int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg
         (topk_indices == 0 || req_pool_indices == 0 || req_host_base == 0 || topk_device_slots == 0 ||
          is_miss == 0 || num_real == 0 || hot_row_base == 0))
         return set_last_error(KVOPS_E_INVALID, "import: a tensor address is 0");
-    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{0, 0, 0};
+    const KvopsRowOpts o = opts ? *opts : KvopsRowOpts{};
     if (o.injective > 1) return set_last_error(KVOPS_E_INVALID, "import: injective must be 0 or 1");
+    if ((o.err_word & 3) != 0) return set_last_error(KVOPS_E_INVALID, "import: err_word must be 4-byte aligned");
     // The launch's scratch is one completion ticket when it publishes status words.
     const size_t need = status != 0 ? sizeof(kvb::Ticket) : 0;
     if (need > KVOPS_NOALLOC_SCRATCH_BYTES)
@@ -126,28 +118,18 @@ extern "C" int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg
     p.st.node_hi = node_num;
     p.st.block_dim = block_dim;
     p.st.ticket = nullptr;
+    p.st.err_word = reinterpret_cast<uint32_t *>(o.err_word);
     if (status != 0) {
-        // The ticket must start at zero: clear it in stream order, then clear the status
-        // words the launch will publish before the launch exists.
+        // The ticket must start at zero: clear it in stream order. The status words the launch
+        // will publish are cleared as every other entry point clears them.
         cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(kvb::Ticket), s);
         if (e != cudaSuccess) {
             cudaGetLastError();
             return set_last_error(KVOPS_E_CUDA, "import_multi_noalloc: cudaMemsetAsync(ticket) failed");
         }
         p.st.ticket = static_cast<kvb::Ticket *>(scratch);
-        if (host_word(status)) {
-            for (uint32_t n = 0; n < node_num; ++n)
-                for (uint32_t b = 0; b < block_dim; ++b)
-                    __atomic_store_n(reinterpret_cast<uint64_t *>(status) + n * 8u + b, 0ull, __ATOMIC_RELEASE);
-        } else {
-            for (uint32_t n = 0; n < node_num; ++n) {
-                e = cudaMemsetAsync(reinterpret_cast<void *>(status + n * 64ull), 0, block_dim * 8ull, s);
-                if (e != cudaSuccess) {
-                    cudaGetLastError();
-                    return set_last_error(KVOPS_E_CUDA, "import_multi_noalloc: cudaMemsetAsync(status) failed");
-                }
-            }
-        }
+        rc = kvb::clear_status_words(status, 0, node_num, block_dim, s);
+        if (rc != KVOPS_OK) return rc;
     }
     cudaError_t e = kvb::launch_gather(p, s, sms);
     if (e != cudaSuccess) {

@@ -1120,7 +1120,7 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
     int32_t mine = 0;              // warp 0: entries of lane's list copied (issued) so far
     bool done_lane = lane >= own;  // warp 0: lane's list is final and every entry taken
     bool finished = false;
-    for (uint32_t iter = 0; iter < (1u << 22) && !finished; ++iter) {
+    for (uint32_t iter = 0; iter < x.wait_polls && !finished; ++iter) {
         if (tid < 32) {
             const int32_t r = cidx + lane * ncopy;
             int32_t avail = 0, cnt = 0;
@@ -1849,8 +1849,8 @@ cudaError_t prepare_sieve_coop(const SieveParams &p)
     return coop_residency(coop_smem(p), &resident);
 }
 
-cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl, cudaStream_t s,
-                              bool *launched)
+cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl,
+                              uint32_t wait_polls, cudaStream_t s, bool *launched)
 {
     *launched = false;
     if (wl == nullptr) return cudaSuccess;  // the copy CTAs move rows only through the walk lists
@@ -1864,6 +1864,7 @@ cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint3
     StepExtra x{};
     x.flags = flags;
     x.wl = wl;
+    x.wait_polls = wait_polls != 0 ? wait_polls : (1u << 22);
     const uint32_t cpr = g.row_bytes / 16;  // helpers copy 16-byte chunks (host-checked)
     x.magic = (cpr > 0 && cpr < 65536 && static_cast<uint64_t>(kFastThreads) * cpr < 65536)
                   ? static_cast<uint32_t>(((1ull << 32) + cpr - 1) / cpr) : 0u;

@@ -3,7 +3,9 @@ captured once and replayed as one graph launch, which removes the per-launch gap
 layers' kernels.
 
 The captured calls publish no status words (there is no host work in a replay to zero them);
-completion is the stream's. Everything a captured call reads is fixed at capture time: the
+completion is the stream's. Device-side errCodes (a row past its segment, a null segment, a
+cooperative copy that stopped waiting) go to one device error word shared by the captured
+calls (KvopsRowOpts.err_word): `error()` reads it after a replay and `clear_error()` resets it. Everything a captured call reads is fixed at capture time: the
 coordinator's batch tensors (`set_batch`), its state tensors and `self.topk` — so a decode loop
 copies each step's top-K indices into `self.topk` (and refreshes the batch tensors in place)
 before `replay()`. The reference has no counterpart (its driver issues the calls one by one,
@@ -41,13 +43,15 @@ class StepGraph:
         # outside the capture.
         k.step_prepare(coord.top_k, coord.device_buffer_size, coord.padded_buffer_size, coord.visited_stride_b,
                        coord.max_num_reqs)
+        self.err = torch.zeros(1, dtype=torch.int32, device=coord.device)
         self.graph = torch.cuda.CUDAGraph()
         self.stream = torch.cuda.Stream(device=coord.device)
         with torch.cuda.graph(self.graph, stream=self.stream):
             s = self.stream.cuda_stream
             for layer in range(self.layers):
                 pool.sieve_and_read(coord, layer, self.topk[layer], hot[layer], s, block_dim,
-                                    hot_req_stride_rows=hot_req_stride_rows, path=path, publish=False)
+                                    hot_req_stride_rows=hot_req_stride_rows, path=path, publish=False,
+                                    err_word=self.err)
                 if after_layer is not None:
                     after_layer(layer)
         self.path = k.last_step_path()
@@ -55,3 +59,11 @@ class StepGraph:
     def replay(self) -> None:
         """Runs the captured step on the current stream."""
         self.graph.replay()
+
+    def error(self) -> int:
+        """First errCode any replay since the last clear_error() recorded (0: none); waits for
+        the replays queued on the current stream."""
+        return int(self.err.item()) & 0xFFFFFFFF
+
+    def clear_error(self) -> None:
+        self.err.zero_()

@@ -10,6 +10,7 @@ owned by node s under the unchanged stripe map node=(row/S)%N, segRow=(row/S)/N
 channels) is replaced by local allocation, peer access, or CUDA IPC handles for segments
 owned by other processes.
 """
+import bisect
 from typing import List, Optional, Sequence
 
 from . import kvops as _kvops_module
@@ -56,54 +57,90 @@ def seg_row_of(row, stripe_rows, node_num, injective=False):
 
 
 class RowAllocator:
-    """Host-side row allocator with the reference's contiguity contract
-    (xds/xds_ems_pool.py:54-106): a contiguous run when one fits, else the lowest free rows."""
+    """Host-side pool-row allocator with the reference's contiguity contract
+    (xds/xds_ems_pool.py:54-106): a request's rows must be contiguous when that is possible,
+    because the gather addresses them as req_host_base + position. alloc(n) returns the first
+    free run (in row order) that holds n rows; when none does, the n lowest free rows.
+
+    Free space is kept as two sorted parallel lists (run starts, run ends), so freeing a row
+    merges it with its neighbours by bisection instead of re-sorting every run. Freeing a row
+    that is already free raises ValueError (the reference would count it twice)."""
 
     def __init__(self, capacity: int):
+        if capacity < 0:
+            raise ValueError("capacity must be >= 0")
         self.capacity = capacity
-        self._runs = [(0, capacity)]  # sorted, disjoint, half-open free runs
-        self._used = 0
+        self._lo: List[int] = [0] if capacity else []  # run starts, ascending
+        self._hi: List[int] = [capacity] if capacity else []  # matching exclusive ends
+        self._nfree = capacity
 
     def alloc(self, n: int) -> List[int]:
         if n <= 0:
             raise ValueError("n must be > 0")
-        if n > self.free_rows():
-            raise MemoryError("allocator exhausted: free={} need={}".format(self.free_rows(), n))
-        for i, (s, e) in enumerate(self._runs):
-            if e - s >= n:
-                self._runs[i:i + 1] = [(s + n, e)] if e - s > n else []
-                self._used += n
-                return list(range(s, s + n))
-        out: List[int] = []
+        if n > self._nfree:
+            raise MemoryError("allocator exhausted: free={} need={}".format(self._nfree, n))
+        self._nfree -= n
+        for i in range(len(self._lo)):
+            lo, hi = self._lo[i], self._hi[i]
+            if hi - lo >= n:  # first run that fits: one contiguous block
+                if hi - lo == n:
+                    del self._lo[i], self._hi[i]
+                else:
+                    self._lo[i] = lo + n
+                return list(range(lo, lo + n))
+        out: List[int] = []  # fragmented: the lowest free rows, whole runs first
         while len(out) < n:
-            s, e = self._runs[0]
-            take = min(e - s, n - len(out))
-            out.extend(range(s, s + take))
-            self._runs[0:1] = [(s + take, e)] if e - s > take else []
-        self._used += n
+            lo, hi = self._lo[0], self._hi[0]
+            take = min(hi - lo, n - len(out))
+            out.extend(range(lo, lo + take))
+            if take == hi - lo:
+                del self._lo[0], self._hi[0]
+            else:
+                self._lo[0] = lo + take
         return out
 
     def free(self, rows: List[int]) -> None:
-        if not rows:
-            return
+        rows = list(rows)
         for r in rows:
             if r < 0 or r >= self.capacity:
                 raise ValueError("row out of range: {}".format(r))
-        runs = sorted(self._runs + [(r, r + 1) for r in rows])
-        merged = []
-        for s, e in runs:
-            if merged and s <= merged[-1][1]:
-                merged[-1] = (merged[-1][0], max(merged[-1][1], e))
-            else:
-                merged.append((s, e))
-        self._runs = merged
-        self._used -= len(rows)
+        if len(set(rows)) != len(rows):
+            raise ValueError("row freed twice in one call")
+        for r in rows:
+            if self._is_free(r):
+                raise ValueError("row {} is not allocated".format(r))
+        for r in sorted(rows):
+            self._insert(r)
+        self._nfree += len(rows)
+
+    def _is_free(self, r: int) -> bool:
+        i = bisect.bisect_right(self._lo, r) - 1
+        return i >= 0 and r < self._hi[i]
+
+    def _insert(self, r: int) -> None:
+        i = bisect.bisect_right(self._lo, r)  # runs [0, i) start at or before r
+        joins_left = i > 0 and self._hi[i - 1] == r
+        joins_right = i < len(self._lo) and self._lo[i] == r + 1
+        if joins_left and joins_right:
+            self._hi[i - 1] = self._hi[i]
+            del self._lo[i], self._hi[i]
+        elif joins_left:
+            self._hi[i - 1] = r + 1
+        elif joins_right:
+            self._lo[i] = r
+        else:
+            self._lo.insert(i, r)
+            self._hi.insert(i, r + 1)
+
+    def free_runs(self) -> List[tuple]:
+        """The free rows as sorted, disjoint, non-adjacent half-open runs."""
+        return list(zip(self._lo, self._hi))
 
     def free_rows(self) -> int:
-        return sum(e - s for s, e in self._runs)
+        return self._nfree
 
     def used_rows(self) -> int:
-        return self._used
+        return self.capacity - self._nfree
 
 
 class DevicePool:
@@ -192,7 +229,7 @@ class DevicePool:
         return status
 
     def sieve_and_read(self, coord, layer_id, topk_indices, hot_row_base, stream=0, block_dim=1, *,
-                       hot_req_stride_rows=0, path="auto", publish=True) -> int:
+                       hot_req_stride_rows=0, path="auto", publish=True, err_word=0, copy_wait_polls=0) -> int:
         """One decode layer-step in one call: `coord.sieve_update(layer_id, topk_indices)`
         followed by `batch_read` of its miss rows from every segment (the reference driver's
         pair, xds_decode.py:225-233), with identical results (kvops_sieve_import). path="auto"
@@ -200,7 +237,10 @@ class DevicePool:
         segment is on another GPU, and the two kernels (the gather launched as a programmatic
         dependent) otherwise; "coop" / "fused" / "split" force one. Returns the status address for
         `wait`, or 0 with publish=False: then no status words are written and completion is
-        observed on the stream (the form a CUDA graph can replay, see graph.StepGraph)."""
+        observed on the stream (the form a CUDA graph can replay, see graph.StepGraph).
+        err_word: address (or int32 tensor) of a word that receives the first device-side
+        errCode by compare-and-swap from 0 (KvopsRowOpts.err_word); copy_wait_polls: bound of a
+        cooperative copy CTA's wait for a walk list (KvopsRowOpts.copy_wait_polls, 0 = default)."""
         import torch
         if topk_indices.dtype != torch.int32:
             raise ValueError("topk_indices must be int32")
@@ -213,7 +253,7 @@ class DevicePool:
             coord.padded_buffer_size, coord.visited_stride_b, coord.max_num_reqs, coord.pool_size, self.seg_bases,
             layer_id * self.per_layer_seg_rows, self.per_layer_seg_rows, self.row_bytes, _ptr(coord.req_host_base),
             _ptr(hot_row_base), self.stripe_rows, status, stream, block_dim, hot_req_stride_rows=hot_req_stride_rows,
-            injective=self.injective, path=path)
+            injective=self.injective, path=path, err_word=_ptr(err_word), copy_wait_polls=copy_wait_polls)
         return status
 
     def batch_write(self, layer_id, topk_indices, req_pool_indices, req_host_base, topk_device_slots, export_flags,

@@ -220,7 +220,9 @@ def layout_fixture(lay, align, compute_ht_size, row_word):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("KVOPS_REFERENCE_DIR") or
+                    os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"),
+                    help="the reference tree (default: $KVOPS_REFERENCE_DIR, else ../reference beside the repo)")
     a = ap.parse_args()
     Oracle, row_word, align, compute_ht_size, lay = _load_ref(a.ref)
     with open(os.path.join(HERE, "sieve_kat.json"), "w") as f:

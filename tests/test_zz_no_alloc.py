@@ -4,11 +4,19 @@ It exists for callers that cannot allocate device memory: an inference engine wh
 is owned by its own allocator or fixed budget, or a decode loop that cannot pay for
 cudaMalloc/cudaFree. Its scratch is a static device array shared by all calls, so the
 test checks two calls in a row against the regular kvops_import_multi, byte for byte, on
-the hot buffer and on every status word. This file is collected last on purpose."""
+the hot buffer and on every status word, and both against the C restatement of the gather.
+A second test runs it first thing in a fresh process (before any other entry point has set
+the device up) and checks that the device's free memory does not move. This file is
+collected last on purpose."""
 import ctypes
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
+
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -16,8 +24,10 @@ RB = 1152
 
 
 class Opts(ctypes.Structure):
+    """KvopsRowOpts (include/kvops_b200.h)."""
     _fields_ = [("hot_req_stride_rows", ctypes.c_uint64), ("injective", ctypes.c_uint32),
-                ("step_path", ctypes.c_uint32)]
+                ("step_path", ctypes.c_uint32), ("err_word", ctypes.c_uint64), ("copy_wait_polls", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
 
 
 def _lib():
@@ -56,7 +66,8 @@ def test_noalloc_gather_matches_regular_two_calls():
     num_real = torch.tensor([R], dtype=torch.int32, device="cuda")
     status = u64()
     assert lib.kvops_alloc_status(8 * N, ctypes.byref(status)) == 0
-    opts = Opts(dbs, 0, 0)
+    opts = Opts(dbs, 0, 0, 0, 0, 0)
+    segs_h = [s.cpu().numpy() for s in segs]
     for call, layer in enumerate((1, 0)):  # two calls in a row share the static scratch
         topk, miss, slots = _batch(torch, 10 + call, R, K, ctx, dbs, N)
         outs, words = [], []
@@ -79,12 +90,78 @@ def test_noalloc_gather_matches_regular_two_calls():
         assert words[0] == words[1] == [0] * (4 * N)
         np.testing.assert_array_equal(outs[1], outs[0])
         assert int(miss.sum()) > 0 and outs[0].any()
+        exp = np.zeros(R * dbs * RB, np.uint8)
+        n = oracle.gather_all(segs_h, layer * plsr, RB, topk.cpu().numpy(), pool.cpu().numpy(), base.cpu().numpy(),
+                              slots.cpu().numpy(), miss.cpu().numpy(), R, exp, K, R, 1, hot_req_stride_rows=dbs)
+        assert n == int(miss.sum())
+        np.testing.assert_array_equal(outs[1], exp)
 
 
 def test_noalloc_rejects_bad_arguments():
     lib = _lib()
     u64 = ctypes.c_uint64
     seg = (u64 * 1)(8)
-    opts = Opts(0, 0, 0)
+    opts = Opts(0, 0, 0, 0, 0, 0)
     rc = lib.kvops_import_multi_noalloc(1, seg, 0, 1, RB, 8, 8, 8, 8, 8, 8, 8, 1, 1, 1, 0, 0, 9, ctypes.byref(opts))
     assert rc == 3 and b"<= 8" in lib.kvops_last_error()
+
+
+_FRESH = r"""
+import ctypes, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+sys.path.insert(0, sys.argv[1] + "/tests")
+import kv_offload_proto_b200 as kp
+import oracle
+from test_zz_no_alloc import Opts, RB
+lib = kp.load_library()
+u64, u32 = ctypes.c_uint64, ctypes.c_uint32
+sig = [u32, ctypes.POINTER(u64), u32, u32, u32] + [u64] * 7 + [u32, u32, u32, u64, u64, u32, ctypes.POINTER(Opts)]
+lib.kvops_import_multi_noalloc.argtypes = sig
+lib.kvops_poll_status.argtypes = [u64, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]
+R, K, ctx, dbs = 4, 128, 1024, 256
+rng = np.random.default_rng(3)
+seg_h = rng.integers(0, 256, R * ctx * RB, dtype=np.uint8)
+topk = np.stack([rng.choice(ctx, K, replace=False) for _ in range(R)]).astype(np.int32)
+miss = (rng.random((R, K)) < 0.5).astype(np.int8)
+slots = np.stack([rng.permutation(dbs)[:K] for _ in range(R)]).astype(np.int32)
+pool, base = np.arange(R, dtype=np.int64), np.arange(R, dtype=np.int64) * ctx
+d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+seg, t_topk, t_miss, t_slots, t_pool, t_base = d(seg_h), d(topk), d(miss), d(slots), d(pool), d(base)
+t_nr = d(np.array([R], np.int32))
+hot = torch.zeros(R * dbs * RB, dtype=torch.uint8, device="cuda")
+status = torch.zeros(64, dtype=torch.int64, device="cuda")  # device-memory status words
+seg_arr = (u64 * 1)(seg.data_ptr())
+opts = Opts(dbs, 0, 0, 0, 0, 0)
+args = (1, seg_arr, 0, R * ctx, RB, t_topk.data_ptr(), t_pool.data_ptr(), t_base.data_ptr(), t_slots.data_ptr(),
+        t_miss.data_ptr(), t_nr.data_ptr(), hot.data_ptr(), K, R, 1, status.data_ptr(), 0, 1, ctypes.byref(opts))
+assert lib.kvops_import_multi_noalloc(*args) == 1, "must require kvops_init"
+assert b"not inited" in lib.kvops_last_error()
+assert lib.kvops_init(0, b"", b"") == 0, lib.kvops_last_error()
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for call in range(2):
+    assert lib.kvops_import_multi_noalloc(*args) == 0, lib.kvops_last_error()
+    out = ctypes.c_int64()
+    assert lib.kvops_poll_status(status.data_ptr(), 10_000_000, ctypes.byref(out)) == 0 and out.value == 0
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+assert free1 == free0, ("device memory moved", free0, free1)
+exp = np.zeros(R * dbs * RB, np.uint8)
+oracle.gather_all([seg_h], 0, RB, topk, pool, base, slots, miss, R, exp, K, R, 1, hot_req_stride_rows=dbs)
+np.testing.assert_array_equal(hot.cpu().numpy(), exp)
+print("fresh-process no-alloc ok", free0 - free1)
+"""
+
+
+def test_noalloc_first_call_in_fresh_process_allocates_nothing():
+    """Run in a child process so that this entry point is the first to touch the device after
+    kvops_init (no ticket ring or scratch set up by earlier tests). Modules load eagerly there,
+    so the library's code and static array are resident before the measurement starts and any
+    allocation the call made would show in cudaMemGetInfo."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    r = subprocess.run([sys.executable, "-c", _FRESH, root], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "fresh-process no-alloc ok 0" in r.stdout
