@@ -109,13 +109,20 @@ def test_noalloc_rejects_bad_arguments():
 _FRESH = r"""
 import ctypes, sys
 import numpy as np
-import torch
+from cuda.bindings import runtime as rt
 sys.path.insert(0, sys.argv[1])
 sys.path.insert(0, sys.argv[1] + "/tests")
 import kv_offload_proto_b200 as kp
 import oracle
 from test_zz_no_alloc import Opts, RB
-lib = kp.load_library()
+
+
+def ck(ret):
+    assert ret[0] == rt.cudaError_t.cudaSuccess, ret
+    return ret[1] if len(ret) == 2 else ret[1:]
+
+
+lib = kp.load_library()  # registers the library's kernels; loaded into the context at creation
 u64, u32 = ctypes.c_uint64, ctypes.c_uint32
 sig = [u32, ctypes.POINTER(u64), u32, u32, u32] + [u64] * 7 + [u32, u32, u32, u64, u64, u32, ctypes.POINTER(Opts)]
 lib.kvops_import_multi_noalloc.argtypes = sig
@@ -127,39 +134,51 @@ topk = np.stack([rng.choice(ctx, K, replace=False) for _ in range(R)]).astype(np
 miss = (rng.random((R, K)) < 0.5).astype(np.int8)
 slots = np.stack([rng.permutation(dbs)[:K] for _ in range(R)]).astype(np.int32)
 pool, base = np.arange(R, dtype=np.int64), np.arange(R, dtype=np.int64) * ctx
-d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+ck(rt.cudaSetDevice(0))
+ck(rt.cudaFree(0))
+
+
+def d(a):  # device copy of a host array (inputs are the caller's, allocated before the measurement)
+    a = np.ascontiguousarray(a)
+    p = ck(rt.cudaMalloc(max(a.nbytes, 8)))
+    ck(rt.cudaMemcpy(p, a.ctypes.data, a.nbytes, rt.cudaMemcpyKind.cudaMemcpyHostToDevice))
+    return p
+
+
 seg, t_topk, t_miss, t_slots, t_pool, t_base = d(seg_h), d(topk), d(miss), d(slots), d(pool), d(base)
 t_nr = d(np.array([R], np.int32))
-hot = torch.zeros(R * dbs * RB, dtype=torch.uint8, device="cuda")
-status = torch.zeros(64, dtype=torch.int64, device="cuda")  # device-memory status words
-seg_arr = (u64 * 1)(seg.data_ptr())
+hot = d(np.zeros(R * dbs * RB, np.uint8))
+status = d(np.zeros(64, np.int64))  # device-memory status words
+seg_arr = (u64 * 1)(seg)
 opts = Opts(dbs, 0, 0, 0, 0, 0)
-args = (1, seg_arr, 0, R * ctx, RB, t_topk.data_ptr(), t_pool.data_ptr(), t_base.data_ptr(), t_slots.data_ptr(),
-        t_miss.data_ptr(), t_nr.data_ptr(), hot.data_ptr(), K, R, 1, status.data_ptr(), 0, 1, ctypes.byref(opts))
+args = (1, seg_arr, 0, R * ctx, RB, t_topk, t_pool, t_base, t_slots, t_miss, t_nr, hot, K, R, 1, status, 0, 1,
+        ctypes.byref(opts))
 assert lib.kvops_import_multi_noalloc(*args) == 1, "must require kvops_init"
 assert b"not inited" in lib.kvops_last_error()
 assert lib.kvops_init(0, b"", b"") == 0, lib.kvops_last_error()
-torch.cuda.synchronize()
-free0 = torch.cuda.mem_get_info()[0]
+ck(rt.cudaDeviceSynchronize())
+free0 = ck(rt.cudaMemGetInfo())[0]
 for call in range(2):
     assert lib.kvops_import_multi_noalloc(*args) == 0, lib.kvops_last_error()
     out = ctypes.c_int64()
-    assert lib.kvops_poll_status(status.data_ptr(), 10_000_000, ctypes.byref(out)) == 0 and out.value == 0
-torch.cuda.synchronize()
-free1 = torch.cuda.mem_get_info()[0]
+    assert lib.kvops_poll_status(status, 10_000_000, ctypes.byref(out)) == 0 and out.value == 0
+ck(rt.cudaDeviceSynchronize())
+free1 = ck(rt.cudaMemGetInfo())[0]
 assert free1 == free0, ("device memory moved", free0, free1)
+got = np.zeros(R * dbs * RB, np.uint8)
+ck(rt.cudaMemcpy(got.ctypes.data, hot, got.nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost))
 exp = np.zeros(R * dbs * RB, np.uint8)
 oracle.gather_all([seg_h], 0, RB, topk, pool, base, slots, miss, R, exp, K, R, 1, hot_req_stride_rows=dbs)
-np.testing.assert_array_equal(hot.cpu().numpy(), exp)
+np.testing.assert_array_equal(got, exp)
 print("fresh-process no-alloc ok", free0 - free1)
 """
 
 
 def test_noalloc_first_call_in_fresh_process_allocates_nothing():
-    """Run in a child process so that this entry point is the first to touch the device after
-    kvops_init (no ticket ring or scratch set up by earlier tests). Modules load eagerly there,
-    so the library's code and static array are resident before the measurement starts and any
-    allocation the call made would show in cudaMemGetInfo."""
+    """Run in a child process (no torch there) so that this entry point is the first to touch
+    the device after kvops_init (no ticket ring or scratch set up by earlier tests). Modules
+    load eagerly there, so the library's code and static array are resident before the
+    measurement starts and any allocation the call made would show in cudaMemGetInfo."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
     r = subprocess.run([sys.executable, "-c", _FRESH, root], env=env, capture_output=True, text=True, timeout=300)
