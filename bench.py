@@ -93,21 +93,24 @@ def peaks():
 
 
 def link_peaks():
-    """NVLink and host-link denominators. profiles/links.json holds this repository's own
-    measurement (`--config link`): the faster of the copy engines and the row kernel on
-    contiguous rows, per direction per GPU. Without it: 770 GB/s, this pool's measured peer copy
-    reference, and 64 GB/s, the PCIe Gen5 x16 nominal per direction."""
+    """NVLink and host-link denominators (GB/s per direction per GPU) with their sources.
+    profiles/links.json holds this repository's own measurement (`--config link`): for NVLink
+    the faster of the copy engines and the row kernel on contiguous peer rows, for the host link
+    the faster of the copy engine and the row kernel reading (or writing) contiguous pinned rows.
+    Without it: 770 GB/s, this pool's measured peer-copy reference, and 64 GB/s, the PCIe Gen5
+    x16 nominal."""
+    out = {"nvlink": (770.0, "pool reference peer copy 770 GB/s per direction"),
+           "host_read": (64.0, "PCIe Gen5 x16 nominal 64 GB/s per direction"),
+           "host_write": (64.0, "PCIe Gen5 x16 nominal 64 GB/s per direction")}
     path = os.path.join(ROOT, "profiles", "links.json")
-    nv, nv_src, hl, hl_src = 770.0, "pool reference peer copy 770 GB/s per direction", 64.0, \
-        "PCIe Gen5 x16 nominal 64 GB/s per direction"
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        if d.get("nvlink_gbs"):
-            nv, nv_src = float(d["nvlink_gbs"]), "measured peer read, profiles/links.json"
-        if d.get("host_link_gbs"):
-            hl, hl_src = float(d["host_link_gbs"]), "measured host read, profiles/links.json"
-    return nv, nv_src, hl, hl_src
+        for key, field in (("nvlink", "nvlink_gbs"), ("host_read", "host_link_gbs"),
+                           ("host_write", "host_link_write_gbs")):
+            if d.get(field):
+                out[key] = (float(d[field]), "measured {} (profiles/links.json)".format(field))
+    return out
 
 
 def cpu_model():
@@ -714,7 +717,7 @@ def roofline(kernel, avg_us, hbm_bytes, link_bytes, link_peak, link_src, link_ki
 
 
 def report_decode(args, cfg, world, gathered, co, L, n_nodes, injective):
-    nv_peak, nv_src, hl_peak, hl_src = link_peaks()
+    lp = link_peaks()
     K = cfg["top_k"]
     elapsed = max(g["elapsed"] for g in gathered)
     miss_rows = sum(g["miss_rows"] for g in gathered)
@@ -731,7 +734,7 @@ def report_decode(args, cfg, world, gathered, co, L, n_nodes, injective):
     sieve_bytes = R * (2 * sb + 9 * K + 16)
     remote = g0["remote_rows"]
     link_kind = "host_link" if args.pool == "host" else "nvlink"
-    link_peak, link_src = (hl_peak, hl_src) if args.pool == "host" else (nv_peak, nv_src)
+    link_peak, link_src = lp["host_read"] if args.pool == "host" else lp["nvlink"]
     rows_remote = rows_per_launch * remote
     rows_local = rows_per_launch - rows_remote
     payload_hbm = rows_local * 2 * ROW_BYTES + rows_remote * ROW_BYTES  # local: read + write; remote: write
@@ -887,7 +890,7 @@ def run_export(args):
     cl.close()
     if rank != 0:
         return
-    nv_peak, nv_src, hl_peak, hl_src = link_peaks()
+    lp = link_peaks()
     tmax = max(g["dev_s"] for g in gathered)
     total_bytes = sum(g["units"] for g in gathered) * ROW_BYTES * Sn
     value = total_bytes / tmax / 1e9
@@ -896,7 +899,7 @@ def run_export(args):
     remote_units = g0["units"] - g0["local_units"]
     hbm_bytes = (g0["units"] + g0["local_units"]) * ROW_BYTES  # every row read; local rows also written here
     link_kind = "host_link" if cl.pinned else "nvlink"
-    link_peak, link_src = (hl_peak, hl_src) if cl.pinned else (nv_peak, nv_src)
+    link_peak, link_src = lp["host_write"] if cl.pinned else lp["nvlink"]
     roof = roofline("export_kernel", per_launch_s * 1e6, hbm_bytes, remote_units * ROW_BYTES, link_peak, link_src,
                     link_kind)
     roof["note"] = "per decode-step-equivalent: the N segment launches of one batch_write_alllayers together"
@@ -1035,8 +1038,21 @@ def run_link(args):
         torch.cuda.synchronize()
         out["host_copy_engine_h2d"] = nbytes * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
         del d
+    with torch.cuda.device(0):  # host write: export_seg_alllayer of nrows contiguous rows into pinned memory
+        src = torch.empty(nrows * ROW_BYTES, dtype=torch.uint8, device="cuda")
+        st0 = torch.cuda.current_stream().cuda_stream
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        mod.export_seg_alllayer(0, hseg, nrows, ROW_BYTES, 0, nrows, 1, src.data_ptr(), 0, 0, 1, 0, 0, st0, 1)
+        e0.record()
+        for _ in range(reps):
+            mod.export_seg_alllayer(0, hseg, nrows, ROW_BYTES, 0, nrows, 1, src.data_ptr(), 0, 0, 1, 0, 0, st0, 1)
+        e1.record()
+        torch.cuda.synchronize()
+        out["host_write_contiguous"] = nrows * ROW_BYTES * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
+        del src
     mod.segment_free(hseg)
     out["host_link_gbs"] = max(out["host_read_contiguous"], out["host_copy_engine_h2d"])
+    out["host_link_write_gbs"] = out["host_write_contiguous"]
     if ngpu >= 2:
         for a in range(ngpu):
             for b in range(ngpu):
@@ -1057,21 +1073,23 @@ def run_link(args):
             out["peer_copy_engine"] = nbytes * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9
             del d
         out["nvlink_gbs"] = max(out["peer_read_contiguous"], out["peer_copy_engine"])
-        if ngpu > 2:  # every GPU reads random rows from every other GPU at once
-            out["all_to_all_random_per_gpu"] = all_to_all(torch, mod, segs, ngpu, nrows, reps)
+        # every GPU at once reads random rows: from all other GPUs, and from one other GPU each
+        out["all_peers_random_per_gpu"] = all_to_all(torch, mod, segs, ngpu, nrows, reps)
+        out["one_peer_random_per_gpu"] = all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=True)
         for a in segs:
             mod.segment_free(a)
     print(json.dumps(out), flush=True)
 
 
-def all_to_all(torch, mod, segs, ngpu, nrows, reps, K=4096):
-    """Each GPU gathers nrows random rows spread over the other GPUs' segments (one launch per
-    GPU per repetition, all GPUs at once); returns per-GPU GB/s."""
+def all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=False, K=4096):
+    """Every GPU at once gathers nrows random rows from other GPUs' segments: from all of them
+    (striped, the pool layout of config 2) or, with one_peer, only from GPU (g + 1) % N. One
+    launch per GPU per repetition; returns per-GPU GB/s."""
     per = []
     setup = []
     for g in range(ngpu):
         with torch.cuda.device(g):
-            others = [segs[h] for h in range(ngpu) if h != g]
+            others = [segs[(g + 1) % ngpu]] if one_peer else [segs[h] for h in range(ngpu) if h != g]
             n = len(others)
             R = (nrows + K - 1) // K
             gen = torch.Generator(device="cuda").manual_seed(g + 11)
@@ -1107,7 +1125,7 @@ def all_to_all(torch, mod, segs, ngpu, nrows, reps, K=4096):
             torch.cuda.synchronize(g)
     for g in range(ngpu):
         R = setup[g][9]
-        per.append(R * 4096 * ROW_BYTES * reps / (evs[g][0].elapsed_time(evs[g][1]) * 1e-3) / 1e9)
+        per.append(R * K * ROW_BYTES * reps / (evs[g][0].elapsed_time(evs[g][1]) * 1e-3) / 1e9)
     return per
 
 
