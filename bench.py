@@ -53,6 +53,8 @@ CONFIGS = {
                stripe_rows=16, seed=7, placement="all", zipf=1.1, injective=True, per_rank_requests=False),
     "c4": dict(name="c4_prefill_export", requests=16, ctx=8192, layers=61, stripe_rows=64, seed=4,
                placement="all", injective=True),
+    "c5": dict(name="c5_sieve_stress", requests=1024, ctx=131072, top_k=2048, dbs=65518, steps=50, seed=123,
+               miss_ratio=0.9, zipf=0.8),
 }
 CFG = CONFIGS["c2"]
 METRIC = "miss-row import GB/s (sieve+gather, per layer-step)"
@@ -65,7 +67,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "link"], default="c2")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5", "link"], default="c2")
+    ap.add_argument("--dist", choices=["uniform", "zipf", "both"], default="both", help="c5: the stress draws")
+    ap.add_argument("--requests", type=int, default=None, help="c5: requests (default: the config's 1024)")
     ap.add_argument("--layers", type=int, default=None, help="layers per decode step (default: the config's)")
     ap.add_argument("--path", choices=["auto", "coop", "fused", "split"], default="auto",
                     help="layer-step path of sieve_and_read (auto: cooperative when it fits)")
@@ -971,6 +975,107 @@ def run_cpu_export(injective):
                 rows, S), "cpu_model": cpu_model()}
 
 
+# ---- SIEVE stress (c5) ------------------------------------------------------------------
+
+def run_stress(args):
+    """BASELINE config 5 on one GPU: 1024 requests, hot buffer 65518 slots, topK 2048, context
+    131072, 50 steps of each stress draw (workload.stress_topk_uniform / stress_topk_zipf, numpy,
+    drawn on the host from the state read back after every step). Every step's slots and miss
+    flags are hashed and compared with the checksum fixture tests/golden/c5_checksums.json,
+    which the C restatement of the reference kernel produced from the same draws
+    (tests/golden/make_c5.py); the final state too. Device time of each sieve_update launch."""
+    import hashlib
+
+    import torch
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    import kv_offload_proto_b200 as kp
+    from kv_offload_proto_b200.offload import XdsOffloadCoordinator
+    from kv_offload_proto_b200.workload import stress_topk_uniform, stress_topk_zipf, zipf_cdf
+    cfg = CONFIGS["c5"]
+    torch.cuda.set_device(local)
+    mod = kp.install_kvops_ext()
+    mod.init(local, "")
+    dev = torch.device("cuda", local)
+    R = args.requests or cfg["requests"]
+    ctx, K, dbs = cfg["ctx"], cfg["top_k"], cfg["dbs"]
+    steps = cfg["steps"] if args.steps == parse_defaults()["steps"] else args.steps
+    fx = None
+    fx_path = os.path.join(ROOT, "tests", "golden", "c5_checksums.json")
+    if os.path.exists(fx_path):
+        with open(fx_path) as f:
+            fx = json.load(f)
+        if fx["config"]["reqs"] != R or fx["config"]["steps"] < steps:
+            fx = None
+
+    def sha(a):
+        return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+    results = {}
+    for dist in (("uniform", "zipf") if args.dist == "both" else (args.dist,)):
+        co = XdsOffloadCoordinator(dev, 1, R, dbs, K, R, ctx)
+        co.admit_all([ctx] * R, [r * ctx for r in range(R)])
+        co.set_batch(torch.arange(R, dtype=torch.int64, device=dev), torch.full((R,), ctx, dtype=torch.int32,
+                                                                                 device=dev))
+        if dist == "uniform":
+            rng = np.random.default_rng(cfg["seed"])
+        else:
+            cdf, perm = zipf_cdf(ctx, cfg["zipf"], cfg["seed"])
+            rng = np.random.default_rng(cfg["seed"] + 1)
+        ref = fx["draws"].get(dist) if fx else None
+        us, matches, misses, tiers = [], 0, 0, set()
+        clocks = ClockSampler(torch, local)
+        clocks.start()
+        for step in range(steps):
+            if dist == "uniform":
+                topk = stress_topk_uniform(rng, co.device_buffer_tokens[0].cpu().numpy(), dbs, ctx, K,
+                                           cfg["miss_ratio"])
+            else:
+                topk = stress_topk_zipf(rng, R, ctx, K, cdf, perm)
+            t = torch.from_numpy(topk).to(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            co.sieve_update(0, t)
+            e1.record()
+            torch.cuda.synchronize()
+            tiers.add(mod.last_sieve_tier())
+            us.append(e0.elapsed_time(e1) * 1e3)
+            slots, miss = co.top_k_device_slots.cpu().numpy(), co.is_miss.cpu().numpy()
+            misses += int(miss.sum())
+            if ref is not None:
+                r = ref["steps"][step]
+                matches += int(r["slots"] == sha(slots) and r["is_miss"] == sha(miss) and r["topk"] == sha(topk))
+        clk = clocks.stop()
+        final = None
+        if ref is not None and steps == len(ref["steps"]):
+            got = {"tokens": sha(co.device_buffer_tokens[0].cpu().numpy()),
+                   "visited": sha(co.device_buffer_visited[0].cpu().numpy()),
+                   "ht": sha(co.device_buffer_ht[0].cpu().numpy().view(np.uint16)),
+                   "hand": sha(co.sieve_hand[0, :, 0].cpu().numpy().copy())}
+            final = got == ref["final"]
+        results[dist] = {"steps": steps, "us_per_step_p50": pct(us, 50), "us_per_step_p99": pct(us, 99),
+                         "us_per_step_mean": sum(us) / len(us), "us_first_step": us[0],
+                         "us_per_request_step": sum(us) / len(us) / R, "miss_ratio": misses / (steps * R * K),
+                         "tiers": sorted(tiers), "checksum_steps_matched": matches if ref is not None else None,
+                         "final_state_matched": final, "clocks": clk}
+        del co
+        torch.cuda.empty_cache()
+    out = {"metric": "SIEVE stress: sieve_update us per step (1024 requests) and bit-exactness vs the CPU model",
+           "value": results[next(iter(results))]["us_per_step_mean"], "unit": "us/step", "n_gpus": 1,
+           "steps": steps, "warmup": 0, "higher_is_better": False, "dtype": "int32", "data": "synthetic",
+           "config": {"workload": cfg["name"], "requests": R, "hot_slots": dbs, "top_k": K, "ctx": ctx,
+                      "ht_cells": 262144, "draws": list(results)},
+           "fixture": os.path.relpath(fx_path, ROOT) if fx is not None else None, "draws": results,
+           "gpu_launches": steps * len(results)}
+    print(json.dumps(out), flush=True)
+
+
+def parse_defaults():
+    """argparse defaults (so a config can tell an explicit --steps from the default)."""
+    return {"steps": 5}
+
+
 # ---- link probe -------------------------------------------------------------------------
 
 def run_link(args):
@@ -1234,6 +1339,8 @@ def main():
         run_link(args)
     elif args.config == "c4":
         run_export(args)
+    elif args.config == "c5":
+        run_stress(args)
     else:
         run_decode(args, CONFIGS[args.config])
 

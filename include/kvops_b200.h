@@ -192,6 +192,29 @@ int kvops_sieve_update(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
                        uint32_t visited_stride_b, uint32_t max_num_reqs, uint32_t pool_size, uint64_t stream,
                        uint32_t block_dim);
 
+/* SIEVE kernel tiers (no counterpart in the reference, whose kernel has one tier and rejects
+ * states over its 176 KB UB budget, kvops_ext.cpp:302-306). Every tier gives the same outputs
+ * and state bytes.
+ * SHARED: the phase-parallel step with the request's state in shared memory (tables up to 65536
+ *   cells that fit, e.g. hot buffers up to ~8K slots).
+ * LARGE: the large-table tier: the same phases with a direct token index and the table updated
+ *   in global memory by run re-packing (any table; one scratch area per device, ~3 MB per SM,
+ *   allocated on the first call of such a shape or by kvops_step_prepare, so launches that use
+ *   it on one device must be ordered: one stream, or ordered by events).
+ * ORDERED: the reference's position-ordered loop, in shared memory when the state fits, else in
+ *   global memory. AUTO: SHARED when it fits, else LARGE, else ORDERED. */
+#define KVOPS_TIER_AUTO 0u
+#define KVOPS_TIER_SHARED 1u
+#define KVOPS_TIER_LARGE 2u
+#define KVOPS_TIER_ORDERED 3u
+
+/* The tier the calling thread's later SIEVE launches use (AUTO by default); a tier that cannot
+ * run a shape falls back to AUTO's choice. */
+int kvops_set_sieve_tier(uint32_t tier);
+
+/* The tier the calling thread's last SIEVE launch ran (AUTO before any). */
+uint32_t kvops_last_sieve_tier(void);
+
 /* Replaces kv_sieve_ht_init + hisp_sieve_ht_init (kvops_ext.cpp:339-358,
  * kvops/kernel/hisp_sieve_ht_init.cpp:14-60). Rebuilds the tables of
  * min(block_dim, layer_num*num_reqs) (layer, request) pairs; block_dim 0 means all. */

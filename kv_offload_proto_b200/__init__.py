@@ -22,7 +22,8 @@ C_ABI_SYMBOLS = (
     "kvops_export_seg_alllayer_ex", "kvops_sieve_update", "kvops_sieve_ht_init", "kvops_segment_alloc",
     "kvops_segment_free", "kvops_enable_peer_access", "kvops_ipc_get_handle", "kvops_ipc_open_handle",
     "kvops_ipc_close_handle", "kvops_import_multi_noalloc", "kvops_sieve_import",
-    "kvops_last_step_path", "kvops_step_prepare", "kvops_export_seg",
+    "kvops_last_step_path", "kvops_step_prepare", "kvops_export_seg", "kvops_set_sieve_tier",
+    "kvops_last_sieve_tier",
 )
 
 _lib = None

@@ -37,7 +37,7 @@ def _run(cmd):
 
 
 def build_lib(force=False, verbose_ptxas=False):
-    deps = [os.path.join(CSRC, f) for f in CU_SOURCES + ["kvops_internal.cuh", "rows_common.cuh"]]
+    deps = [os.path.join(CSRC, f) for f in CU_SOURCES + ["kvops_internal.cuh", "rows_common.cuh", "sieve_big.cuh"]]
     deps.append(os.path.join(ROOT, "include", "kvops_b200.h"))
     if not force and not _newer(LIB, deps):
         return LIB

@@ -48,6 +48,9 @@ struct DeviceState {
     uint2 *wl = nullptr;         // cooperative layer-steps: kWalkListBufs walk-list buffers
     size_t wl_entries = 0;       // entries per buffer
     std::vector<uint2 *> wl_old;  // outgrown buffers (a captured graph may still name one)
+    uint8_t *big = nullptr;      // large-table SIEVE tier: zeroed scratch (the kernel leaves it zero)
+    size_t big_bytes = 0;
+    std::vector<uint8_t *> big_old;  // outgrown scratch (a captured graph may still name one)
 };
 
 // Words of cooperative layer-steps: launch n uses block n % kReadyBlocks, so a block is reused
@@ -58,6 +61,7 @@ constexpr uint32_t kReadyBlocks = 1024, kReadyWords = kvb::kCoopBlockWords, kWal
 
 std::mutex g_mu;
 thread_local uint32_t t_last_step_path = KVOPS_STEP_AUTO;  // path the last kvops_sieve_import ran
+thread_local uint32_t t_tier_choice = KVOPS_TIER_AUTO;      // kvops_set_sieve_tier of this thread
 bool g_inited = false;
 int g_home_device = 0;
 std::vector<void *> g_status_allocs;
@@ -283,6 +287,8 @@ int export_common(uint64_t seg_base, uint32_t plsr, uint32_t row_bytes, uint32_t
     return KVOPS_OK;
 }
 
+int attach_big_scratch(DeviceState *ds, kvb::SieveParams *p);
+
 int build_sieve(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_lens, uint64_t prefill_lens,
                        uint64_t device_buffer_tokens, uint64_t device_buffer_visited, uint64_t device_buffer_ht,
                        uint64_t sieve_hand, uint64_t topk_device_slots, uint64_t is_miss, uint64_t num_real,
@@ -336,6 +342,8 @@ int build_sieve(uint64_t topk_indices, uint64_t req_pool_indices, uint64_t seq_l
     p.pool_size = static_cast<int32_t>(pool_size);
     p.ht_size = static_cast<int32_t>(ht_size);
     (void)stream;
+    rc = attach_big_scratch(ds, &p);
+    if (rc != KVOPS_OK) return rc;
     *out = p;
     *ds_out = ds;
     return KVOPS_OK;
@@ -380,6 +388,39 @@ int ensure_walk_lists(DeviceState *ds, size_t entries)
     if (ds->wl != nullptr) ds->wl_old.push_back(ds->wl);
     ds->wl = w;
     ds->wl_entries = entries;
+    return KVOPS_OK;
+}
+
+// Grows (once per shape, never shrinking) the large-table tier's scratch to `bytes`, zeroed.
+int ensure_big_scratch(DeviceState *ds, size_t bytes)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ds->big != nullptr && ds->big_bytes >= bytes) return KVOPS_OK;
+    uint8_t *b = nullptr;
+    cudaError_t e = cudaMalloc(&b, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(large-table SIEVE scratch)");
+    e = cudaMemset(b, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(b);
+        return cuda_fail(e, "cudaMemset(large-table SIEVE scratch)");
+    }
+    if (ds->big != nullptr) ds->big_old.push_back(ds->big);
+    ds->big = b;
+    ds->big_bytes = bytes;
+    return KVOPS_OK;
+}
+
+// Points the launch at the large-table tier's scratch when its shape uses that tier.
+int attach_big_scratch(DeviceState *ds, kvb::SieveParams *p)
+{
+    int32_t slots = 0;
+    const uint64_t slot_bytes = kvb::sieve_big_scratch(*p, ds->sm_count, &slots);
+    if (slots <= 0) return KVOPS_OK;
+    const int rc = ensure_big_scratch(ds, static_cast<size_t>(slot_bytes) * slots);
+    if (rc != KVOPS_OK) return rc;
+    p->big = ds->big;
+    p->big_slot_bytes = slot_bytes;
+    p->big_slots = slots;
     return KVOPS_OK;
 }
 
@@ -480,6 +521,8 @@ int kvops_close(void)
         if (kv.second->ready) cudaFree(kv.second->ready);
         if (kv.second->wl) cudaFree(kv.second->wl);
         for (uint2 *w : kv.second->wl_old) cudaFree(w);
+        if (kv.second->big) cudaFree(kv.second->big);
+        for (uint8_t *b : kv.second->big_old) cudaFree(b);
         delete kv.second;
     }
     g_devices.clear();
@@ -692,7 +735,9 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
     const uint32_t path = opts ? opts->step_path : KVOPS_STEP_AUTO;
     if (path > KVOPS_STEP_COOP) return fail(KVOPS_E_INVALID, "sieve_import: step_path must be 0, 1, 2 or 3");
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (sds != nullptr && (path == KVOPS_STEP_AUTO || path == KVOPS_STEP_COOP) && vec16_ok(gp)) {
+    // The one-kernel paths run the shared-memory tier; another chosen tier runs as SPLIT.
+    const bool shared_tier = t_tier_choice == KVOPS_TIER_AUTO || t_tier_choice == KVOPS_TIER_SHARED;
+    if (sds != nullptr && shared_tier && (path == KVOPS_STEP_AUTO || path == KVOPS_STEP_COOP) && vec16_ok(gp)) {
         uint32_t *words = nullptr;
         uint2 *wl = nullptr;
         rc = next_ready_block(sds, static_cast<size_t>(max_num_reqs) * top_k, &words, &wl);
@@ -706,7 +751,7 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
         }
     }
     bool remote = false;
-    if (sds != nullptr && path == KVOPS_STEP_FUSED && bulk_copy_ok(gp, &remote)) {
+    if (sds != nullptr && shared_tier && path == KVOPS_STEP_FUSED && bulk_copy_ok(gp, &remote)) {
         bool launched = false;
         cudaError_t e = kvb::launch_sieve_import(sp, gp, st, &launched);
         if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import");
@@ -728,6 +773,16 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
 
 uint32_t kvops_last_step_path(void) { return t_last_step_path; }
 
+int kvops_set_sieve_tier(uint32_t tier)
+{
+    if (tier > KVOPS_TIER_ORDERED) return fail(KVOPS_E_INVALID, "set_sieve_tier: tier must be 0, 1, 2 or 3");
+    t_tier_choice = tier;
+    kvb::set_sieve_tier(tier);
+    return KVOPS_OK;
+}
+
+uint32_t kvops_last_sieve_tier(void) { return kvb::last_sieve_tier(); }
+
 int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t padded_buffer_size,
                        uint32_t visited_stride_b, uint32_t max_num_reqs)
 {
@@ -748,6 +803,8 @@ int kvops_step_prepare(uint32_t top_k, uint32_t device_buffer_size, uint32_t pad
     p.vis_stride = static_cast<int32_t>(visited_stride_b);
     p.max_num_reqs = static_cast<int32_t>(max_num_reqs);
     p.ht_size = static_cast<int32_t>(ht_size);
+    rc = attach_big_scratch(ds, &p);
+    if (rc != KVOPS_OK) return rc;
     cudaError_t e = kvb::prepare_sieve_coop(p);
     if (e != cudaSuccess) return cuda_fail(e, "step_prepare");
     return KVOPS_OK;

@@ -63,6 +63,9 @@ struct SieveParams {
     int8_t *is_miss;            // [max_num_reqs, top_k]
     const int32_t *num_real;    // [1]
     int32_t top_k, dbs, padded, vis_stride, max_num_reqs, pool_size, ht_size;
+    uint8_t *big;               // large-table tier: global scratch, big_slots slots (nullptr: tier unavailable)
+    uint64_t big_slot_bytes;
+    int32_t big_slots;
 };
 
 struct HtInitParams {
@@ -156,6 +159,15 @@ bool is_inited();
 // Zeroes the status words [node_lo, node_hi) x [0, block_dim) at `status` before a launch
 // publishes them: pinned host words by the host now, device words on `stream` (capi.cu).
 int clear_status_words(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint32_t block_dim, cudaStream_t stream);
+
+// SIEVE tiers (KVOPS_TIER_*): the caller's choice for the calling thread, and the tier its last
+// launch_sieve_update ran.
+void set_sieve_tier(uint32_t tier);
+uint32_t last_sieve_tier();
+// Bytes of one slot of the large-table tier's scratch and the slots it needs (*slots = 0: the
+// shape does not use that tier under the calling thread's choice). The scratch must be zero
+// when first used; the kernel leaves it zero again.
+uint64_t sieve_big_scratch(const SieveParams &p, int sm_count, int32_t *slots);
 
 // Kernel launchers (defined next to their kernels).
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int sm_count);

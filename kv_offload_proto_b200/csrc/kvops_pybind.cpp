@@ -235,6 +235,24 @@ PYBIND11_MODULE(_kvops, m)
             default: return std::string("none");
         }
     });
+    // SIEVE tier of this thread's later launches, and the tier of its last one (not in the reference module).
+    m.def("set_sieve_tier", [](const std::string &tier) {
+        uint32_t t;
+        if (tier == "auto") t = KVOPS_TIER_AUTO;
+        else if (tier == "shared") t = KVOPS_TIER_SHARED;
+        else if (tier == "large") t = KVOPS_TIER_LARGE;
+        else if (tier == "ordered") t = KVOPS_TIER_ORDERED;
+        else throw std::invalid_argument("set_sieve_tier: tier must be 'auto', 'shared', 'large' or 'ordered'");
+        check(kvops_set_sieve_tier(t));
+    }, py::arg("tier"));
+    m.def("last_sieve_tier", []() {
+        switch (kvops_last_sieve_tier()) {
+            case KVOPS_TIER_SHARED: return std::string("shared");
+            case KVOPS_TIER_LARGE: return std::string("large");
+            case KVOPS_TIER_ORDERED: return std::string("ordered");
+            default: return std::string("none");
+        }
+    });
     m.def("sieve_ht_init", &sieve_ht_init, py::arg("device_buffer_tokens"), py::arg("device_buffer_ht"),
           py::arg("prefill_lens"), py::arg("req_start"), py::arg("num_reqs"), py::arg("layer_num"),
           py::arg("pool_size"), py::arg("device_buffer_size"), py::arg("padded_buffer_size"), py::arg("ht_size"),

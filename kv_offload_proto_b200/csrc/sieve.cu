@@ -1736,6 +1736,11 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     }
 }
 
+#include "sieve_big.cuh"
+
+thread_local uint32_t t_tier_choice = KVOPS_TIER_AUTO;  // caller's choice (kvops_set_sieve_tier)
+thread_local uint32_t t_tier_last = KVOPS_TIER_AUTO;    // tier of the last launch_sieve_update
+
 int max_optin_smem()
 {
     int dev = 0, v = 0;
@@ -1746,20 +1751,68 @@ int max_optin_smem()
 
 }  // namespace
 
+void set_sieve_tier(uint32_t tier) { t_tier_choice = tier; }
+uint32_t last_sieve_tier() { return t_tier_last; }
+
+namespace {
+
+bool shared_tier_fits(const SieveParams &p, int limit)
+{
+    if (p.top_k > 65535 || p.ht_size > 65536 || p.dbs > 65535) return false;  // 16-bit bookkeeping
+    return fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs).total <= static_cast<size_t>(limit);
+}
+
+bool large_tier_fits(const SieveParams &p, int limit)
+{
+    if (p.top_k > 65535 || p.dbs > 65534 || p.ht_size < 1024) return false;
+    return big_layout(p.ht_size, p.vis_stride, p.top_k, p.dbs).total <= static_cast<size_t>(limit);
+}
+
+// The tier a launch of this shape runs under the calling thread's choice.
+uint32_t pick_tier(const SieveParams &p, int limit, bool large_scratch)
+{
+    const bool shared = shared_tier_fits(p, limit);
+    const bool large = large_tier_fits(p, limit) && large_scratch;
+    if (t_tier_choice == KVOPS_TIER_ORDERED) return KVOPS_TIER_ORDERED;
+    if (t_tier_choice == KVOPS_TIER_LARGE && large) return KVOPS_TIER_LARGE;
+    if (t_tier_choice == KVOPS_TIER_SHARED && shared) return KVOPS_TIER_SHARED;
+    return shared ? KVOPS_TIER_SHARED : large ? KVOPS_TIER_LARGE : KVOPS_TIER_ORDERED;
+}
+
+}  // namespace
+
+uint64_t sieve_big_scratch(const SieveParams &p, int sm_count, int32_t *slots)
+{
+    *slots = 0;
+    if (p.max_num_reqs <= 0 || p.top_k <= 0) return 0;
+    if (pick_tier(p, max_optin_smem(), true) != KVOPS_TIER_LARGE) return 0;
+    const int32_t sms = sm_count > 0 ? sm_count : 148;
+    *slots = p.max_num_reqs < sms ? p.max_num_reqs : sms;
+    return big_slot(p.dbs, p.padded).bytes;
+}
+
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int /*sm_count*/)
 {
     if (p.max_num_reqs <= 0) return cudaSuccess;
     const int limit = max_optin_smem();
-    // Parallel path: positions and slots must fit its 16-bit bookkeeping.
-    if (p.top_k <= 65535 && p.ht_size <= 65536 && p.dbs <= 65535) {
+    const uint32_t tier = pick_tier(p, limit, p.big != nullptr && p.big_slots > 0);
+    t_tier_last = tier;
+    if (tier == KVOPS_TIER_SHARED) {
         const FastLayout F = fast_layout(p.padded, p.ht_size, p.vis_stride, p.top_k, p.dbs);
-        if (F.total <= static_cast<size_t>(limit)) {
-            cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(F.total));
-            if (e != cudaSuccess) return e;
-            sieve_fast_kernel<0><<<p.max_num_reqs, kFastThreads, F.total, s>>>(p, GatherParams{}, StepExtra{});
-            return cudaGetLastError();
-        }
+        cudaError_t e = cudaFuncSetAttribute(sieve_fast_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(F.total));
+        if (e != cudaSuccess) return e;
+        sieve_fast_kernel<0><<<p.max_num_reqs, kFastThreads, F.total, s>>>(p, GatherParams{}, StepExtra{});
+        return cudaGetLastError();
+    }
+    if (tier == KVOPS_TIER_LARGE) {
+        const BigLayout B = big_layout(p.ht_size, p.vis_stride, p.top_k, p.dbs);
+        cudaError_t e = cudaFuncSetAttribute(sieve_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(B.total));
+        if (e != cudaSuccess) return e;
+        const int grid = p.max_num_reqs < p.big_slots ? p.max_num_reqs : p.big_slots;
+        sieve_big_kernel<<<grid, kBigThreads, B.total, s>>>(p);
+        return cudaGetLastError();
     }
     const SmemLayout L = sieve_smem_layout(p.padded, p.ht_size, p.vis_stride, p.top_k);
     if (L.total <= static_cast<size_t>(limit)) {

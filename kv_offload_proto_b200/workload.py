@@ -5,14 +5,17 @@
 * ``sample_topk_device``: the BASELINE configs' draw on the GPU — unique positions per request,
   hits drawn from the tokens currently resident in the hot buffer (read from the device SIEVE
   state), misses from non-resident prefill positions, optionally weighted by a finite Zipf pmf.
+* ``stress_topk_uniform`` / ``stress_topk_zipf``: the SIEVE stress config's host draws
+  numpy only, so the same seed and state give the same positions wherever
+  they are drawn (the checksum fixture of the CPU model and the GPU run).
 * ``row_word`` / ``fill_fingerprint``: the reference's row fingerprint (xds/xds_decode.py:18,60-63).
 """
 import numpy as np
 
 P1, P2, M1, M2 = 0x9E3779B1, 0x85EBCA77, 0x27220A95, 0x165667B1
 
-__all__ = ["ref_topk_batch", "sample_topk_device", "zipf_pmf", "row_word", "fingerprint_rows", "P1", "P2", "M1",
-           "M2"]
+__all__ = ["ref_topk_batch", "sample_topk_device", "zipf_pmf", "stress_topk_uniform", "stress_topk_zipf",
+           "row_word", "fingerprint_rows", "P1", "P2", "M1", "M2"]
 
 
 def ref_topk_batch(rng, req_num, top_k, prefill, dbs, miss_ratio):
@@ -40,6 +43,64 @@ def zipf_pmf(n, s, perm_seed):
     p = np.empty(n, dtype=np.float64)
     p[perm] = w
     return p
+
+
+def stress_topk_uniform(rng, tokens_rows, dbs, ctx, top_k, miss_ratio):
+    """[R, top_k] int32: per request, round(miss_ratio * top_k) distinct positions drawn
+    uniformly from the positions of [0, ctx) that are not resident in its token row
+    (tokens_rows[r, :dbs]) and the rest from the resident ones, in shuffled order. One uniform
+    key per position; the smallest keys of each group win (buffers are reused across rows)."""
+    R = tokens_rows.shape[0]
+    out = np.empty((R, top_k), np.int32)
+    n_miss = int(round(miss_ratio * top_k))
+    n_hit = top_k - n_miss
+    keys, grp = np.empty(ctx), np.empty(ctx)
+    res = np.zeros(ctx, bool)
+    for r in range(R):
+        tok = tokens_rows[r, :dbs]
+        res[:] = False
+        res[tok[(tok >= 0) & (tok < ctx)]] = True
+        nres = int(np.count_nonzero(res))
+        if nres < n_hit or ctx - nres < n_miss:
+            raise ValueError("stress_topk_uniform: too few resident or non-resident positions")
+        rng.random(out=keys)
+        np.copyto(grp, keys)
+        grp[res] = np.inf
+        m = np.sort(np.argpartition(grp, n_miss - 1)[:n_miss]) if n_miss else np.empty(0, np.int64)
+        np.copyto(grp, keys)
+        grp[~res] = np.inf
+        h = np.sort(np.argpartition(grp, n_hit - 1)[:n_hit]) if n_hit else np.empty(0, np.int64)
+        row = np.concatenate([m, h])
+        out[r] = row[rng.permutation(top_k)]
+    return out
+
+
+def stress_topk_zipf(rng, R, ctx, top_k, cdf, perm):
+    """[R, top_k] int32: per request, the first top_k distinct positions of a stream of draws
+    from the finite Zipf pmf whose cumulative sums are `cdf` (cdf[-1] == 1) over the ranks,
+    mapped to positions by the permutation `perm` (zipf_pmf's construction). The popularity
+    does not depend on the state, so the miss ratio follows from the SIEVE itself."""
+    out = np.empty((R, top_k), np.int32)
+    for r in range(R):
+        chosen = np.empty(0, np.int64)
+        seen = np.zeros(ctx, bool)
+        while chosen.size < top_k:
+            pos = perm[np.searchsorted(cdf, rng.random(2 * top_k), side="right")]
+            _, first = np.unique(pos, return_index=True)
+            pos = pos[np.sort(first)]
+            pos = pos[~seen[pos]]
+            seen[pos] = True
+            chosen = np.concatenate([chosen, pos[:top_k - chosen.size]])
+        out[r] = chosen
+    return out
+
+
+def zipf_cdf(n, s, perm_seed):
+    """(cdf over ranks with cdf[-1] == 1, rank -> position permutation) of zipf_pmf(n, s)."""
+    w = np.arange(1, n + 1, dtype=np.float64) ** (-float(s))
+    cdf = np.cumsum(w / w.sum())
+    cdf[-1] = 1.0
+    return cdf, np.random.default_rng(perm_seed).permutation(n)
 
 
 def sample_topk_device(tokens_layer, prefill, dbs, top_k, miss_ratio, generator, log_pmf=None):
