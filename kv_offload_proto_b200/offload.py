@@ -7,6 +7,8 @@ HBM with the reference's tensor layout (xds/xds_offload.py:43-53) and every upda
 through the `_kvops` launch module (sieve_ht_init / sieve_update); nothing here runs the
 SIEVE on the host.
 """
+import contextlib
+
 import torch
 
 from . import kvops as _kvops_module
@@ -31,10 +33,12 @@ def compute_ht_size(padded_buffer_size, top_k):
 class XdsOffloadCoordinator:
     """Per-layer SIEVE state and decode-step driver for one device."""
 
+    _require_cuda = True  # the kernels take device addresses (a host-only test subclass may lift this)
+
     def __init__(self, device, layer_num, pool_size, device_buffer_size, top_k, max_num_reqs, max_context_len):
         self._k = _kvops_module()
         self.device = torch.device(device)
-        if self.device.type != "cuda":
+        if self._require_cuda and self.device.type != "cuda":
             raise ValueError("XdsOffloadCoordinator needs a CUDA device, got {}".format(device))
         self.layer_num = layer_num
         self.pool_size = pool_size
@@ -61,7 +65,10 @@ class XdsOffloadCoordinator:
         self._seq_lens = None
 
     def _stream(self):
-        return torch.cuda.current_stream(self.device).cuda_stream
+        return torch.cuda.current_stream(self.device).cuda_stream if self.device.type == "cuda" else 0
+
+    def _on_device(self):
+        return torch.cuda.device(self.device) if self.device.type == "cuda" else contextlib.nullcontext()
 
     def admit_request(self, req_batch_idx, req_pool_idx, prefill_len, host_base_row):
         """Identity admission: slot s holds token s for s < min(prefill, dbs), then the
@@ -71,7 +78,7 @@ class XdsOffloadCoordinator:
         if not 0 <= req_batch_idx < self.max_num_reqs:
             raise ValueError("req_batch_idx out of range: {}".format(req_batch_idx))
         n = min(prefill_len, self.device_buffer_size)
-        with torch.cuda.device(self.device):
+        with self._on_device():
             self.device_buffer_tokens[:, req_pool_idx, :] = -1
             self.device_buffer_tokens[:, req_pool_idx, :n] = torch.arange(n, dtype=torch.int32, device=self.device)
             self.device_buffer_visited[:, req_pool_idx, :].zero_()
@@ -87,7 +94,7 @@ class XdsOffloadCoordinator:
         """Admit pool rows 0..n-1 (batch row r = pool row r) with one table build."""
         n = len(prefill_lens)
         pre = torch.as_tensor(prefill_lens, dtype=torch.int32, device=self.device)
-        with torch.cuda.device(self.device):
+        with self._on_device():
             idx = torch.arange(self.padded_buffer_size, dtype=torch.int32, device=self.device)
             lim = torch.clamp(pre, max=self.device_buffer_size)[:, None]
             rows = torch.where(idx[None, :] < lim, idx[None, :], torch.full_like(idx[None, :], -1))
