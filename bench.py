@@ -69,7 +69,8 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=["c2", "c3", "c4", "c5", "link"], default="c2")
     ap.add_argument("--dist", choices=["uniform", "zipf", "both"], default="both", help="c5: the stress draws")
-    ap.add_argument("--requests", type=int, default=None, help="c5: requests (default: the config's 1024)")
+    ap.add_argument("--requests", type=int, default=None,
+                    help="requests per GPU (default: the config's; smaller only for profiling captures)")
     ap.add_argument("--layers", type=int, default=None, help="layers per decode step (default: the config's)")
     ap.add_argument("--path", choices=["auto", "coop", "fused", "split"], default="auto",
                     help="layer-step path of sieve_and_read (auto: cooperative when it fits)")
@@ -368,7 +369,7 @@ def run_decode(args, cfg):
     mod = kp.install_kvops_ext()
     mod.init(local, "")
     dev = torch.device("cuda", local)
-    R = cfg["requests"] if cfg["per_rank_requests"] else cfg["requests"] // world
+    R = args.requests or (cfg["requests"] if cfg["per_rank_requests"] else cfg["requests"] // world)
     ctx, K, dbs, miss = cfg["ctx"], cfg["top_k"], cfg["dbs"], cfg["miss_ratio"]
     L = args.layers or cfg["layers"]
     S = cfg["stripe_rows"]
