@@ -74,8 +74,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="layers per decode step (default: the config's)")
     ap.add_argument("--path", choices=["auto", "coop", "fused", "split"], default="auto",
                     help="layer-step path of sieve_and_read (auto: cooperative when it fits)")
-    ap.add_argument("--pool", choices=["hbm", "host"], default="hbm",
-                    help="pool segments in GPU HBM (placement of the config) or in pinned host memory")
+    ap.add_argument("--pool", choices=["hbm", "host", "peer"], default="hbm",
+                    help="pool segments in GPU HBM (placement of the config), in pinned host memory, or (one "
+                         "process only) in the next GPU's HBM through peer access")
     ap.add_argument("--reference-map", action="store_true",
                     help="c3/c4: the reference's segment rows (S>1 stripes share one row) instead of injective rows")
     ap.add_argument("--no-graph", action="store_true",
@@ -245,7 +246,7 @@ class Cluster:
 
         import torch.distributed as dist
         self.rank, self.world, self.local = dist_env()
-        self.pinned = False  # pool segments in pinned host memory
+        self.seg_dev = self.local  # device whose memory holds the segments this rank hosts (-1: pinned host)
         torch.cuda.set_device(self.local)
         self.dist = dist
         if self.world > 1:
@@ -267,23 +268,38 @@ class Cluster:
             self.dist.destroy_process_group()
 
 
-def build_pool(mod, torch, cl, L, plsr, n_nodes, seed, placement, on_host, fill=True):
+def set_pool_kind(torch, mod, cl, kind):
+    """Where the segments this rank hosts live: its own HBM, its pinned host memory, or (one
+    process only) the next GPU's HBM, mapped through peer access."""
+    if kind == "host":
+        cl.seg_dev = -1
+    elif kind == "peer":
+        if cl.world != 1 or torch.cuda.device_count() < 2:
+            raise SystemExit("--pool peer needs one process and two visible GPUs")
+        cl.seg_dev = (cl.local + 1) % torch.cuda.device_count()
+        mod.enable_peer_access(cl.local, cl.seg_dev)
+    else:
+        cl.seg_dev = cl.local
+
+
+def build_pool(mod, torch, cl, L, plsr, n_nodes, seed, placement, fill=True):
     """Segments of this rank's pool (kv_offload_proto_b200.cluster): every rank allocates and
     fills the segments it hosts and maps its own pool's segments through CUDA IPC handles.
-    on_host: every segment of the rank's pool in its own pinned host memory instead.
+    cl.seg_dev < 0: every segment of the rank's pool in its own pinned host memory instead;
+    cl.seg_dev another GPU (one process): the pool's one segment there, read through peer access.
     Returns (segment addresses in node order, node devices, {(owner, node): hosted address},
     opened IPC mappings)."""
     from kv_offload_proto_b200.cluster import hosted_segments, pool_nodes
     from kv_offload_proto_b200.pool import device_view
     seg_bytes = L * plsr * ROW_BYTES
-    dev = "cuda:{}".format(cl.local)
+    dev = "cuda:{}".format(cl.local if cl.seg_dev < 0 else cl.seg_dev)
 
-    def filled(owner, idx, device):
-        addr = mod.segment_alloc(device, seg_bytes)
+    def filled(owner, idx):
+        addr = mod.segment_alloc(cl.seg_dev, seg_bytes)
         if fill:
             gen = torch.Generator(device=dev).manual_seed(seed * 7919 + owner * 131 + idx)
             chunk = 1 << 28
-            if device >= 0:
+            if cl.seg_dev >= 0:  # drawn by the GPU that holds the segment, in its own memory
                 view = device_view(addr, seg_bytes, dev).view(torch.float16)
                 for o in range(0, view.numel(), chunk):
                     view[o:o + chunk].normal_(generator=gen)
@@ -295,12 +311,12 @@ def build_pool(mod, torch, cl, L, plsr, n_nodes, seed, placement, on_host, fill=
                     host[o:o + n].copy_(torch.empty(n, dtype=torch.float16, device=dev).normal_(generator=gen))
         return addr
 
-    if on_host:
-        hosted = {(cl.rank, i): filled(cl.rank, i, -1) for i in range(n_nodes)}
-        return [hosted[(cl.rank, i)] for i in range(n_nodes)], [-1] * n_nodes, hosted, []
+    if cl.seg_dev != cl.local:  # pinned host segments, or the peer GPU's: this rank's own, no exchange
+        hosted = {(cl.rank, i): filled(cl.rank, i) for i in range(n_nodes)}
+        return [hosted[(cl.rank, i)] for i in range(n_nodes)], [cl.seg_dev] * n_nodes, hosted, []
     nodes = pool_nodes(cl.rank, cl.world, placement)
     assert len(nodes) == n_nodes
-    hosted = {(owner, idx): filled(owner, idx, cl.local) for owner, idx in hosted_segments(cl.rank, cl.world, placement)}
+    hosted = {(owner, idx): filled(owner, idx) for owner, idx in hosted_segments(cl.rank, cl.world, placement)}
     if cl.world == 1:
         return [hosted[(cl.rank, 0)]], nodes, hosted, []
     handles = {k: mod.ipc_get_handle(a) for k, a in hosted.items()}
@@ -331,11 +347,11 @@ def read_hosted_rows(torch, cl, hosted, asks, seg_bytes):
             idx = np.asarray(offs, np.int64)
             if (idx < 0).any() or ((idx + 1) * ROW_BYTES > seg_bytes).any():
                 raise RuntimeError("verify: row offset outside the segment")
-            if cl.pinned:
+            if cl.seg_dev < 0:
                 base = np.ctypeslib.as_array((ctypes.c_uint8 * seg_bytes).from_address(addr))
                 out[(asker,) + key] = base.reshape(-1, ROW_BYTES)[idx].copy()
-            else:
-                view = device_view(addr, seg_bytes, "cuda:{}".format(cl.local)).view(-1, ROW_BYTES)
+            else:  # read by the GPU whose memory it is
+                view = device_view(addr, seg_bytes, "cuda:{}".format(cl.seg_dev)).view(-1, ROW_BYTES)
                 out[(asker,) + key] = view[torch.as_tensor(idx, device=view.device)].cpu().numpy()
     return out
 
@@ -359,7 +375,6 @@ def exchange_rows(torch, cl, hosted, ask, seg_bytes):
 def run_decode(args, cfg):
     import torch
     cl = Cluster(torch)
-    cl.pinned = args.pool == "host"
     rank, world, local = cl.rank, cl.world, cl.local
     import kv_offload_proto_b200 as kp
     from kv_offload_proto_b200.offload import XdsOffloadCoordinator
@@ -368,6 +383,7 @@ def run_decode(args, cfg):
 
     mod = kp.install_kvops_ext()
     mod.init(local, "")
+    set_pool_kind(torch, mod, cl, args.pool)
     dev = torch.device("cuda", local)
     R = args.requests or (cfg["requests"] if cfg["per_rank_requests"] else cfg["requests"] // world)
     ctx, K, dbs, miss = cfg["ctx"], cfg["top_k"], cfg["dbs"], cfg["miss_ratio"]
@@ -381,8 +397,7 @@ def run_decode(args, cfg):
     W, Sn = args.warmup, args.steps
     T = W + Sn
 
-    seg_addrs, nodes, hosted, opened = build_pool(mod, torch, cl, L, plsr, n_nodes, cfg["seed"], cfg["placement"],
-                                                  cl.pinned)
+    seg_addrs, nodes, hosted, opened = build_pool(mod, torch, cl, L, plsr, n_nodes, cfg["seed"], cfg["placement"])
     pool = DevicePool(local, L, layer_rows, ROW_BYTES, S, segment_devices=nodes, segment_addrs=seg_addrs,
                       injective=injective)
     assert pool.per_layer_seg_rows == plsr
@@ -526,7 +541,7 @@ def run_decode(args, cfg):
                clocks=clk, nodes=len(nodes), fused=fused, path=path, graph=bool(graphs), launches=len(kev),
                per_call={"ms_per_step": elapsed_pc * 1e3 / Sn, "clocks": clk_pc}, rank=rank, R=R,
                errors={"device_err_word": device_err, "graph_err_word": graph_err}, verify=verify,
-               remote_rows=remote_fraction(cfg, world, n_nodes, nodes, local, cl.pinned))
+               remote_rows=remote_fraction(nodes, local))
     gathered = cl.all_gather(res)
     graphs = None
     for a in opened:
@@ -540,10 +555,9 @@ def run_decode(args, cfg):
         report_decode(args, cfg, world, gathered, co, L, n_nodes, injective)
 
 
-def remote_fraction(cfg, world, n_nodes, nodes, local, pinned):
-    """Share of the pool's rows that are not in this GPU's HBM (rows are striped evenly)."""
-    if pinned:
-        return 1.0
+def remote_fraction(nodes, local):
+    """Share of the pool's rows that are not in this GPU's HBM (rows are striped evenly over the
+    nodes; a node on device -1 is pinned host memory)."""
     return sum(1 for d in nodes if d != local) / float(len(nodes))
 
 
@@ -763,6 +777,8 @@ def report_decode(args, cfg, world, gathered, co, L, n_nodes, injective):
     call_all = [x for g in gathered for x in g["call_us"]]
     step_all = [x / L for g in gathered for x in g["step_us"]] if g0["graph"] else call_all
     pool_desc = ("pinned host memory, {} segment(s)".format(n_nodes) if args.pool == "host" else
+                 "one segment in the next GPU's HBM, read through peer access (one process)"
+                 if args.pool == "peer" else
                  "local HBM segment" if world == 1 else
                  "striped over the other {} GPUs' HBM".format(world - 1) if cfg["placement"] == "others" else
                  "striped over all {} GPUs' HBM (own included)".format(world))
@@ -832,12 +848,13 @@ def run_export(args):
     import torch
     cfg = CONFIGS["c4"]
     cl = Cluster(torch)
-    cl.pinned = args.pool == "host"
     rank, world, local = cl.rank, cl.world, cl.local
     import kv_offload_proto_b200 as kp
     from kv_offload_proto_b200.pool import DevicePool, per_layer_seg_rows, per_layer_seg_rows_injective
     mod = kp.install_kvops_ext()
     mod.init(local, "")
+    set_pool_kind(torch, mod, cl, args.pool)
+    pinned = cl.seg_dev < 0
     dev = torch.device("cuda", local)
     L = args.layers or cfg["layers"]
     rows = cfg["requests"] * cfg["ctx"]
@@ -845,8 +862,7 @@ def run_export(args):
     injective = cfg["injective"] and not args.reference_map
     N = world
     plsr = per_layer_seg_rows_injective(rows, S, N) if injective else per_layer_seg_rows(rows, N)
-    seg_addrs, nodes, hosted, opened = build_pool(mod, torch, cl, L, plsr, N, cfg["seed"], "all", cl.pinned,
-                                                  fill=False)
+    seg_addrs, nodes, hosted, opened = build_pool(mod, torch, cl, L, plsr, N, cfg["seed"], "all", fill=False)
     pool = DevicePool(local, L, rows, ROW_BYTES, S, segment_devices=nodes, segment_addrs=seg_addrs,
                       injective=injective)
     src = torch.empty((L, rows * ROW_BYTES // 2), dtype=torch.float16, device=dev)
@@ -857,7 +873,7 @@ def run_export(args):
     # Destination rows written per segment: every row (injective), or one per stripe (the
     # reference's map, where the last row of each stripe wins).
     units = rows * L if injective else ((rows + S - 1) // S) * L
-    local_units = sum(1 for d in nodes if d == local) * units / N if not cl.pinned else 0
+    local_units = sum(1 for d in nodes if d == local) * units / N
     W, Sn = args.warmup, args.steps
 
     def step():
@@ -903,8 +919,8 @@ def run_export(args):
     per_launch_s = g0["dev_s"] / Sn  # N launches per step (one per segment)
     remote_units = g0["units"] - g0["local_units"]
     hbm_bytes = (g0["units"] + g0["local_units"]) * ROW_BYTES  # every row read; local rows also written here
-    link_kind = "host_link" if cl.pinned else "nvlink"
-    link_peak, link_src = lp["host_write"] if cl.pinned else lp["nvlink"]
+    link_kind = "host_link" if pinned else "nvlink"
+    link_peak, link_src = lp["host_write"] if pinned else lp["nvlink"]
     roof = roofline("export_kernel", per_launch_s * 1e6, hbm_bytes, remote_units * ROW_BYTES, link_peak, link_src,
                     link_kind)
     roof["note"] = "per decode-step-equivalent: the N segment launches of one batch_write_alllayers together"
@@ -914,7 +930,8 @@ def run_export(args):
            "dtype": "u8", "data": "synthetic",
            "config": {"workload": cfg["name"], "rows_per_layer": rows, "layers": L, "row_bytes": ROW_BYTES,
                       "stripe_rows": S, "segment_rows": "injective" if injective else "reference map",
-                      "nodes": N, "pool": "pinned host memory" if cl.pinned else "HBM of all {} GPUs".format(world),
+                      "nodes": N, "pool": "pinned host memory" if pinned else
+                      "the next GPU's HBM (peer access)" if args.pool == "peer" else "HBM of all {} GPUs".format(world),
                       "l2": "inputs larger than L2 ({:.2f} GB source per GPU)".format(L * stride / 1e9),
                       "step": "one EmsPool.batch_write_alllayers: {} kvops_export_seg_alllayer launches".format(N)},
            "bytes_per_step_per_rank": g0["units"] * ROW_BYTES,
