@@ -743,7 +743,11 @@ int kvops_sieve_import(uint64_t topk_indices, uint64_t req_pool_indices, uint64_
         rc = next_ready_block(sds, static_cast<size_t>(max_num_reqs) * top_k, &words, &wl);
         if (rc != KVOPS_OK) return rc;
         bool launched = false;
-        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, wl, opts ? opts->copy_wait_polls : 0u, st, &launched);
+        // AUTO takes the cooperative step only when the copy CTAs number at least half the
+        // requests; with fewer, the full-GPU gather after the SIEVE kernel moves the rows faster.
+        const int32_t min_copy = path == KVOPS_STEP_AUTO ? static_cast<int32_t>(max_num_reqs / 2) : 8;
+        cudaError_t e = kvb::launch_sieve_coop(sp, gp, words, wl, opts ? opts->copy_wait_polls : 0u, min_copy, st,
+                                               &launched);
         if (e != cudaSuccess) return cuda_fail(e, "launch sieve_import (cooperative)");
         if (launched) {
             t_last_step_path = KVOPS_STEP_COOP;

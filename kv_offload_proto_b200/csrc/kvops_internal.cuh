@@ -185,11 +185,12 @@ cudaError_t launch_sieve_import(const SieveParams &p, const GatherParams &g, cud
 // walk list (wl: max_num_reqs x top_k entries) as the hand sweep makes them final, and every
 // other CTA resident on the GPU copies the listed rows (progress words in `flags`, a
 // zero-initialised block of kCoopBlockWords words that no other launch uses while this one
-// runs). *launched = false (nothing launched) when wl is null, fewer than 8 copy CTAs fit
-// beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
+// runs). *launched = false (nothing launched) when wl is null, fewer than max(8, min_copy_ctas)
+// copy CTAs fit beside the SIEVE CTAs, there are more than 252 requests, or the state does not fit.
 // wait_polls: walk-list polls of a copy CTA before it reports KVOPS_ERR_COPY_TIMEOUT (0: 2^22).
+// min_copy_ctas: launch only if at least this many copy CTAs (and never fewer than 8) fit.
 cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl,
-                              uint32_t wait_polls, cudaStream_t s, bool *launched);
+                              uint32_t wait_polls, int32_t min_copy_ctas, cudaStream_t s, bool *launched);
 // Sets up, without launching, what the first cooperative step of this shape would: the
 // kernel's shared-memory limit and the cached residency (so a later call may be captured).
 cudaError_t prepare_sieve_coop(const SieveParams &p);

@@ -1101,62 +1101,60 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
     return m0;
 }
 
-// Copy CTA cidx of ncopy during the walks: follows the walk lists of requests cidx, cidx +
-// ncopy, ... (lane i of warp 0 polls the i-th; there are at most 32 since ncopy >= 8), copying
-// each list's published entries in order, until every list it follows is final and copied.
-__device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t num_real,
+constexpr int kCopyBlock = 128;  // walk-list entries per copy unit
+
+// Copy CTA cidx of ncopy during the walks. The work is cut into units u = b * nr + r: block b
+// (kCopyBlock entries) of request r's walk list. CTA cidx takes its units u = cidx, cidx + ncopy,
+// ... in order: a unit is copied once its entries are listed (or its list is final), and skipped
+// once the final list ends before it. Consecutive blocks of one request go to different CTAs,
+// so every copy CTA has work whether there are more requests than copy CTAs or fewer, and a
+// request's rows are copied by several CTAs at once. Ends when its units run past the lists.
+__device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t nr,
                                 int32_t K, int32_t cidx, int32_t ncopy)
 {
-    __shared__ int32_t s_r, s_t0, s_t1;
-    __shared__ int s_wn, s_last;
-    const unsigned kAll = 0xFFFFFFFFu;
+    __shared__ int32_t s_state, s_t1;
+    __shared__ int64_t s_u;
+    __shared__ int s_wn;
     const unsigned tid = threadIdx.x, nt = blockDim.x;
-    const int lane = tid & 31;
     const uint8_t **srcl = reinterpret_cast<const uint8_t **>(smem);
     uint8_t **dstl = reinterpret_cast<uint8_t **>(smem + 8 * nt);
-    const int32_t own = cidx < num_real ? min((num_real - cidx + ncopy - 1) / ncopy, 32) : 0;
-    if (own == 0) return;
+    if (nr <= 0 || K <= 0) return;
+    const int64_t nunits = static_cast<int64_t>((K + kCopyBlock - 1) / kCopyBlock) * nr;
+    int64_t u = cidx;  // thread 0's cursor
     if (tid == 0) s_wn = 0;
-    int32_t mine = 0;              // warp 0: entries of lane's list copied (issued) so far
-    bool done_lane = lane >= own;  // warp 0: lane's list is final and every entry taken
-    bool finished = false;
+    bool finished = u >= nunits;
     for (uint32_t iter = 0; iter < x.wait_polls && !finished; ++iter) {
-        if (tid < 32) {
-            const int32_t r = cidx + lane * ncopy;
-            int32_t avail = 0, cnt = 0;
-            bool fin = false;
-            if (!done_lane) {
+        if (tid == 0) {
+            int32_t state = 0, t1 = 0;
+            for (int guard = 0; guard < 64 && u < nunits; ++guard) {  // skip units past final lists
+                const int32_t r = static_cast<int32_t>(u % nr), lo = static_cast<int32_t>(u / nr) * kCopyBlock;
                 const int32_t pv = wl_probe(x, r);
-                cnt = pv < 0 ? 0 : (pv >> 1);
-                fin = pv >= 0 && (pv & 1) != 0;
-                avail = cnt - mine;
-                if (fin && avail <= 0) done_lane = true;
-            }
-            const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
-            if (best > 0) {
-                const int pick = __ffs(__ballot_sync(kAll, avail == best)) - 1;
-                if (lane == pick) {
-                    s_r = r;
-                    s_t0 = mine;
-                    s_t1 = mine + min(best, static_cast<int32_t>(nt));
-                    mine = s_t1;
-                    if (fin && mine >= cnt) done_lane = true;  // this chunk ends a final list
+                const int32_t cnt = pv < 0 ? 0 : (pv >> 1);
+                const bool fin = pv >= 0 && (pv & 1) != 0;
+                if (fin && cnt <= lo) {
+                    u += ncopy;
+                    continue;
                 }
+                if (cnt >= lo + kCopyBlock || (fin && cnt > lo)) {
+                    state = 1;
+                    t1 = min(cnt, lo + kCopyBlock);
+                }
+                break;
             }
-            // Every list done once this chunk (if any) is copied: no further poll is needed.
-            const bool all_done = __ballot_sync(kAll, done_lane) == kAll;
-            if (lane == 0) {
-                if (best == 0) s_r = all_done ? -2 : -1;
-                s_last = best > 0 && all_done ? 1 : 0;
-            }
+            if (u >= nunits) state = 2;
+            s_state = state;
+            s_t1 = t1;
+            s_u = u;
+            if (state == 1) u += ncopy;
         }
         __syncthreads();
-        const int32_t r = s_r;
-        if (r == -2) {
+        const int32_t st = s_state;
+        if (st == 2) {
             finished = true;
-        } else if (r >= 0) {
-            if (s_last) finished = true;  // after this copy
-            const int32_t t0 = s_t0, t1 = s_t1;
+        } else if (st == 1) {
+            const int64_t uu = s_u;
+            const int32_t r = static_cast<int32_t>(uu % nr), t0 = static_cast<int32_t>(uu / nr) * kCopyBlock;
+            const int32_t t1 = s_t1;
             const uint8_t *src = nullptr;
             uint8_t *dst = nullptr;
             bool ok = false;
@@ -1903,7 +1901,7 @@ cudaError_t prepare_sieve_coop(const SieveParams &p)
 }
 
 cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint32_t *flags, uint2 *wl,
-                              uint32_t wait_polls, cudaStream_t s, bool *launched)
+                              uint32_t wait_polls, int32_t min_copy_ctas, cudaStream_t s, bool *launched)
 {
     *launched = false;
     if (wl == nullptr) return cudaSuccess;  // the copy CTAs move rows only through the walk lists
@@ -1913,7 +1911,7 @@ cudaError_t launch_sieve_coop(const SieveParams &p, const GatherParams &g, uint3
     int resident = 0;
     cudaError_t e = coop_residency(total, &resident);
     if (e != cudaSuccess) return e;
-    if (resident - p.max_num_reqs < 8) return cudaSuccess;
+    if (resident - p.max_num_reqs < (min_copy_ctas > 8 ? min_copy_ctas : 8)) return cudaSuccess;
     StepExtra x{};
     x.flags = flags;
     x.wl = wl;

@@ -36,18 +36,18 @@ def test_reference_call_sequence_on_the_gpu():
         np.testing.assert_array_equal(topk, fx["topk"][s])
         np.testing.assert_array_equal(slots, fx["slots"][s])
         np.testing.assert_array_equal(miss, fx["is_miss"][s])
-    # the last step of each layer left its miss rows in hbm[layer] (shared hot rows: only slots
-    # named by one position of that step are determined)
+    # The last step of each layer left its miss rows in hbm[layer]. The reference's hot rows are
+    # shared by all requests (hot_row_base + slot), so a slot several positions name ends up
+    # holding one of their rows, unspecified which (the reference's launch order decides): each
+    # such slot must hold exactly one of its candidates' fingerprints.
     for s in (len(steps) - 2, len(steps) - 1):
         topk, slots, miss = steps[s]
         layer = s % 2
-        r_idx, k_idx = np.nonzero(miss)
-        sl = slots[r_idx, k_idx]
-        uniq, cnt = np.unique(sl, return_counts=True)
-        for r, k, slot in zip(r_idx, k_idx, sl):
-            if cnt[np.searchsorted(uniq, slot)] != 1:
-                continue
-            row = bases[r] + int(topk[r, k])
-            np.testing.assert_array_equal(hbm_h[layer, slot], fingerprint_rows([row], layer, RB // 4)[0])
+        cands = {}
+        for r, k in zip(*np.nonzero(miss)):
+            cands.setdefault(int(slots[r, k]), []).append(bases[r] + int(topk[r, k]))
+        for slot, rows in cands.items():
+            fps = fingerprint_rows(rows, layer, RB // 4)
+            assert any(np.array_equal(hbm_h[layer, slot], fp) for fp in fps), (s, slot)
             checked += 1
-    assert checked > 50
+    assert checked >= 32
