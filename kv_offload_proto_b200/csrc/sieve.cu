@@ -1101,68 +1101,81 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
     return m0;
 }
 
-constexpr int kCopyBlock = 128;  // walk-list entries per copy unit
-
-// Copy CTA cidx of ncopy during the walks. The work is cut into units u = b * nr + r: block b
-// (kCopyBlock entries) of request r's walk list. CTA cidx takes its units u = cidx, cidx + ncopy,
-// ... in order: a unit is copied once its entries are listed (or its list is final), and skipped
-// once the final list ends before it. Consecutive blocks of one request go to different CTAs,
-// so every copy CTA has work whether there are more requests than copy CTAs or fewer, and a
-// request's rows are copied by several CTAs at once. Ends when its units run past the lists.
+// Copy CTA cidx of ncopy during the walks. The work is cut into units u = b * nr + r: block b of
+// request r's walk list, nb blocks per request, sized so that every CTA holds at most 32 units
+// (nb = min(32 * ncopy / nr, K / 256), at least 1). CTA cidx holds units cidx, cidx + ncopy, ...;
+// lane i of warp 0 polls the list of the i-th, and each round the CTA copies the published
+// entries of the unit with the most waiting (up to one per thread), until every unit it holds
+// is final and copied. With more requests than copy CTAs a unit is a whole request; with fewer,
+// a request's blocks spread over several CTAs, so no copy CTA idles.
 __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t nr,
                                 int32_t K, int32_t cidx, int32_t ncopy)
 {
-    __shared__ int32_t s_state, s_t1;
-    __shared__ int64_t s_u;
-    __shared__ int s_wn;
+    __shared__ int32_t s_r, s_t0, s_t1;
+    __shared__ int s_wn, s_last;
+    const unsigned kAll = 0xFFFFFFFFu;
     const unsigned tid = threadIdx.x, nt = blockDim.x;
+    const int lane = tid & 31;
     const uint8_t **srcl = reinterpret_cast<const uint8_t **>(smem);
     uint8_t **dstl = reinterpret_cast<uint8_t **>(smem + 8 * nt);
     if (nr <= 0 || K <= 0) return;
-    const int64_t nunits = static_cast<int64_t>((K + kCopyBlock - 1) / kCopyBlock) * nr;
-    int64_t u = cidx;  // thread 0's cursor
+    int32_t nb = static_cast<int32_t>((32ll * ncopy) / nr);
+    nb = min(nb, (K + 255) / 256);
+    if (nb < 1) nb = 1;
+    const int32_t blk = (K + nb - 1) / nb;
+    const int64_t nunits = static_cast<int64_t>(nb) * nr;
+    const int64_t u = static_cast<int64_t>(cidx) + static_cast<int64_t>(lane) * ncopy;  // lane's unit (warp 0)
+    const int32_t r = static_cast<int32_t>(u % nr);
+    const int32_t lo = static_cast<int32_t>(u / nr) * blk, hi = min(lo + blk, K);
     if (tid == 0) s_wn = 0;
-    bool finished = u >= nunits;
+    int32_t mine = lo;                   // warp 0: entries of the lane's unit copied (issued) so far
+    bool done_lane = u >= nunits;        // warp 0: the lane's unit is final and every entry taken
+    bool finished = false;
     for (uint32_t iter = 0; iter < x.wait_polls && !finished; ++iter) {
-        if (tid == 0) {
-            int32_t state = 0, t1 = 0;
-            for (int guard = 0; guard < 64 && u < nunits; ++guard) {  // skip units past final lists
-                const int32_t r = static_cast<int32_t>(u % nr), lo = static_cast<int32_t>(u / nr) * kCopyBlock;
+        if (tid < 32) {
+            int32_t avail = 0, end = hi;
+            bool fin = false;
+            if (!done_lane) {
                 const int32_t pv = wl_probe(x, r);
                 const int32_t cnt = pv < 0 ? 0 : (pv >> 1);
-                const bool fin = pv >= 0 && (pv & 1) != 0;
-                if (fin && cnt <= lo) {
-                    u += ncopy;
-                    continue;
-                }
-                if (cnt >= lo + kCopyBlock || (fin && cnt > lo)) {
-                    state = 1;
-                    t1 = min(cnt, lo + kCopyBlock);
-                }
-                break;
+                fin = pv >= 0 && (pv & 1) != 0;
+                end = min(cnt, hi);
+                avail = end - mine;
+                if (fin && avail <= 0) done_lane = true;
             }
-            if (u >= nunits) state = 2;
-            s_state = state;
-            s_t1 = t1;
-            s_u = u;
-            if (state == 1) u += ncopy;
+            const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
+            if (best > 0) {
+                const int pick = __ffs(__ballot_sync(kAll, avail == best)) - 1;
+                if (lane == pick) {
+                    s_r = r;
+                    s_t0 = mine;
+                    s_t1 = mine + min(best, static_cast<int32_t>(nt));
+                    mine = s_t1;
+                    if (fin && mine >= end) done_lane = true;  // this chunk ends a final unit
+                }
+            }
+            // Every unit done once this chunk (if any) is copied: no further poll is needed.
+            const bool all_done = __ballot_sync(kAll, done_lane) == kAll;
+            if (lane == 0) {
+                if (best == 0) s_r = all_done ? -2 : -1;
+                s_last = best > 0 && all_done ? 1 : 0;
+            }
         }
         __syncthreads();
-        const int32_t st = s_state;
-        if (st == 2) {
+        const int32_t rr = s_r;
+        if (rr == -2) {
             finished = true;
-        } else if (st == 1) {
-            const int64_t uu = s_u;
-            const int32_t r = static_cast<int32_t>(uu % nr), t0 = static_cast<int32_t>(uu / nr) * kCopyBlock;
-            const int32_t t1 = s_t1;
+        } else if (rr >= 0) {
+            if (s_last) finished = true;  // after this copy
+            const int32_t t0 = s_t0, t1 = s_t1;
             const uint8_t *src = nullptr;
             uint8_t *dst = nullptr;
             bool ok = false;
             if (t0 + static_cast<int32_t>(tid) < t1) {
-                const uint2 e = __ldcg(x.wl + static_cast<int64_t>(r) * K + t0 + tid);
+                const uint2 e = __ldcg(x.wl + static_cast<int64_t>(rr) * K + t0 + tid);
                 const int32_t pos = static_cast<int32_t>(e.y >> 16), slot = static_cast<int32_t>(e.y & 0xFFFFu);
-                ok = gather_eval(g, static_cast<int64_t>(r) * K + pos, 1, static_cast<int32_t>(e.x), slot,
-                                 g.req_pool[r], g.host_base[r], &src, &dst);
+                ok = gather_eval(g, static_cast<int64_t>(rr) * K + pos, 1, static_cast<int32_t>(e.x), slot,
+                                 g.req_pool[rr], g.host_base[rr], &src, &dst);
             }
             list_append(ok, src, dst, srcl, dstl, &s_wn);
             __syncthreads();
