@@ -1101,13 +1101,15 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
     return m0;
 }
 
-// Copy CTA cidx of ncopy during the walks. The work is cut into units u = b * nr + r: block b of
-// request r's walk list, nb blocks per request, sized so that every CTA holds at most 32 units
-// (nb = min(32 * ncopy / nr, K / 256), at least 1). CTA cidx holds units cidx, cidx + ncopy, ...;
-// lane i of warp 0 polls the list of the i-th, and each round the CTA copies the published
-// entries of the unit with the most waiting (up to one per thread), until every unit it holds
-// is final and copied. With more requests than copy CTAs a unit is a whole request; with fewer,
-// a request's blocks spread over several CTAs, so no copy CTA idles.
+constexpr int kCopyChunk = 256;  // walk-list entries per chunk when a request's list is shared
+
+// Copy CTA cidx of ncopy during the walks. The work is cut into units u = j * nr + r: share j of
+// request r's walk list, nb shares per request (nb = ncopy / nr when there are at least two copy
+// CTAs per request, else 1). Share j holds the list's chunks of kCopyChunk entries j, j + nb, ...
+// (all of it when nb = 1), so the shares stay even whatever the list's final length. CTA cidx
+// holds units cidx, cidx + ncopy, ... (at most 32: nr <= 252 and ncopy >= 8); lane i of warp 0
+// polls the list of the i-th, and each round the CTA copies the published entries of the unit
+// with the most waiting (up to one per thread), until every unit it holds is final and copied.
 __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t nr,
                                 int32_t K, int32_t cidx, int32_t ncopy)
 {
@@ -1119,29 +1121,26 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
     const uint8_t **srcl = reinterpret_cast<const uint8_t **>(smem);
     uint8_t **dstl = reinterpret_cast<uint8_t **>(smem + 8 * nt);
     if (nr <= 0 || K <= 0) return;
-    int32_t nb = static_cast<int32_t>((32ll * ncopy) / nr);
-    nb = min(nb, (K + 255) / 256);
-    if (nb < 1) nb = 1;
-    const int32_t blk = (K + nb - 1) / nb;
+    const int32_t nb = ncopy >= 2 * nr ? ncopy / nr : 1;
+    const int32_t chunk = nb > 1 ? kCopyChunk : K;  // nb = 1: the whole list is one chunk
     const int64_t nunits = static_cast<int64_t>(nb) * nr;
     const int64_t u = static_cast<int64_t>(cidx) + static_cast<int64_t>(lane) * ncopy;  // lane's unit (warp 0)
-    const int32_t r = static_cast<int32_t>(u % nr);
-    const int32_t lo = static_cast<int32_t>(u / nr) * blk, hi = min(lo + blk, K);
+    const int32_t r = static_cast<int32_t>(u % nr), share = static_cast<int32_t>(u / nr);
     if (tid == 0) s_wn = 0;
-    int32_t mine = lo;                   // warp 0: entries of the lane's unit copied (issued) so far
+    int32_t ck = share;                  // warp 0: the lane's current chunk
+    int32_t mine = ck * chunk;           // warp 0: next entry of that chunk to copy
     bool done_lane = u >= nunits;        // warp 0: the lane's unit is final and every entry taken
     bool finished = false;
     for (uint32_t iter = 0; iter < x.wait_polls && !finished; ++iter) {
         if (tid < 32) {
-            int32_t avail = 0, end = hi;
+            int32_t avail = 0, cnt = 0;
             bool fin = false;
             if (!done_lane) {
                 const int32_t pv = wl_probe(x, r);
-                const int32_t cnt = pv < 0 ? 0 : (pv >> 1);
+                cnt = pv < 0 ? 0 : (pv >> 1);
                 fin = pv >= 0 && (pv & 1) != 0;
-                end = min(cnt, hi);
-                avail = end - mine;
-                if (fin && avail <= 0) done_lane = true;
+                avail = min(cnt, (ck + 1) * chunk) - mine;
+                if (fin && mine >= cnt) done_lane = true;
             }
             const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
             if (best > 0) {
@@ -1151,7 +1150,11 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
                     s_t0 = mine;
                     s_t1 = mine + min(best, static_cast<int32_t>(nt));
                     mine = s_t1;
-                    if (fin && mine >= end) done_lane = true;  // this chunk ends a final unit
+                    if (mine >= (ck + 1) * chunk) {  // chunk done: the share's next one
+                        ck += nb;
+                        mine = ck * chunk;
+                    }
+                    if (fin && mine >= cnt) done_lane = true;  // this chunk ends a final unit
                 }
             }
             // Every unit done once this chunk (if any) is copied: no further poll is needed.
@@ -1792,14 +1795,33 @@ uint32_t pick_tier(const SieveParams &p, int limit, bool large_scratch)
 
 }  // namespace
 
+// CTAs of the large-table tier resident per SM at this shape (0: cannot launch).
+int big_ctas_per_sm(const SieveParams &p)
+{
+    const BigLayout B = big_layout(p.ht_size, p.vis_stride, p.top_k, p.dbs);
+    if (cudaFuncSetAttribute(sieve_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(B.total)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sieve_big_kernel, kBigThreads, B.total) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return per_sm;
+}
+
 uint64_t sieve_big_scratch(const SieveParams &p, int sm_count, int32_t *slots)
 {
     *slots = 0;
     if (p.max_num_reqs <= 0 || p.top_k <= 0) return 0;
     if (pick_tier(p, max_optin_smem(), true) != KVOPS_TIER_LARGE) return 0;
-    const int32_t sms = sm_count > 0 ? sm_count : 148;
-    *slots = p.max_num_reqs < sms ? p.max_num_reqs : sms;
-    return big_slot(p.dbs, p.padded).bytes;
+    const int32_t per_sm = big_ctas_per_sm(p);
+    if (per_sm <= 0) return 0;  // the tier is not used: launch_sieve_update falls back
+    const int32_t resident = (sm_count > 0 ? sm_count : 148) * per_sm;
+    *slots = p.max_num_reqs < resident ? p.max_num_reqs : resident;
+    return big_slot(p.dbs, p.padded, p.top_k).bytes;
 }
 
 cudaError_t launch_sieve_update(const SieveParams &p, cudaStream_t s, int /*sm_count*/)

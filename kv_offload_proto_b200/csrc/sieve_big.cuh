@@ -25,24 +25,23 @@
 //     (the reference's interleaved erase / insert sequence ends in the same table, since every
 //     erase leaves the table as if its key had never been inserted).
 // "First empty cell from" is answered by a bitmap of empty cells in shared memory (32 KB for
-// 262144 cells). One CTA per SM loops over the requests; each CTA owns one slot of global
-// scratch, allocated once per shape by the host (sieve_big_scratch_bytes).
+// 262144 cells). CTAs of 256 threads (two per SM at the stress shape: the serial re-pack of one
+// leaves the SM's issue slots to the other) loop over the requests; each CTA owns one slot of
+// global scratch, allocated once per shape by the host (sieve_big_scratch).
 
-constexpr int kBigThreads = kFastThreads;
+constexpr int kBigThreads = 256;
 constexpr uint32_t kNoCell = 0xFFFFFFFFu;
 constexpr int32_t kBigIdxCap = 1 << 20;  // tokens [0, kBigIdxCap) are indexed directly
 
 // Shared memory of one CTA (one request at a time).
 struct BigLayout {
-    size_t vini, vfin, topk, os, om, cls, aux, missb, posl, dkey, dfirst, wofs, freeb, delb, total;
-    int32_t dcap, fwords;
+    size_t vini, vfin, topk, os, om, cls, aux, missb, posl, freeb, delb, total;
+    int32_t fwords;
 };
 
 __host__ __device__ __forceinline__ BigLayout big_layout(int32_t ht_size, int32_t vis_stride, int32_t K, int32_t dbs)
 {
     BigLayout L;
-    L.dcap = 1;
-    while (L.dcap < 2 * K) L.dcap <<= 1;
     L.fwords = ht_size / 32;
     size_t o = 0;
     L.vini = take(&o, static_cast<size_t>(vis_stride));
@@ -54,29 +53,34 @@ __host__ __device__ __forceinline__ BigLayout big_layout(int32_t ht_size, int32_
     L.aux = take(&o, 2ull * K);
     L.missb = take(&o, 4ull * ((K + 31) / 32));
     L.posl = take(&o, 2ull * K);
-    L.dkey = take(&o, 4ull * L.dcap);  // phase 1 dedup keys; phase 4 list of run leads
-    L.dfirst = take(&o, 4ull * L.dcap);
-    L.wofs = take(&o, 4ull * ((dbs + 31) / 32 + 1));
     L.freeb = take(&o, 4ull * L.fwords);  // bit set: the cell is empty
     L.delb = take(&o, 4ull * L.fwords);   // phase 0: last empty cell before each word; phase 4: deleted cells
     L.total = o;
     return L;
 }
 
-// Global scratch of one CTA: the token index (zero between requests), and the per-slot arrays.
+// Global scratch of one CTA: the token index (zero between requests), the per-slot arrays, the
+// de-duplication table of phase 1 (then the list of run leads of phase 4) and the word offsets
+// of the candidate list.
 struct BigSlot {
-    size_t idx, tf, cellof, cand, evt, bytes;
+    size_t idx, tf, cellof, cand, evt, dkey, dfirst, wofs, bytes;
+    int32_t dcap;
 };
 
-__host__ __device__ __forceinline__ BigSlot big_slot(int32_t dbs, int32_t padded)
+__host__ __device__ __forceinline__ BigSlot big_slot(int32_t dbs, int32_t padded, int32_t K)
 {
     BigSlot S;
+    S.dcap = 1;
+    while (S.dcap < 2 * K) S.dcap <<= 1;
     size_t o = 0;
     S.idx = take(&o, 2ull * kBigIdxCap);
     S.tf = take(&o, 4ull * dbs);
     S.cellof = take(&o, 4ull * dbs);
     S.cand = take(&o, 4ull * dbs + 16);
     S.evt = take(&o, 2ull * padded);
+    S.dkey = take(&o, 4ull * S.dcap);
+    S.dfirst = take(&o, 4ull * S.dcap);
+    S.wofs = take(&o, 4ull * ((dbs + 31) / 32 + 1));
     S.bytes = align_up(o, 256);
     return S;
 }
@@ -170,7 +174,7 @@ __device__ __forceinline__ int32_t big_block_exclusive_max(int32_t v, int32_t *w
     return max(before, lane == 0 ? -1 : ex_in_warp);
 }
 
-__global__ void __launch_bounds__(kBigThreads, 1) sieve_big_kernel(const SieveParams p)
+__global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SieveParams p)
 {
     // Lets a programmatic dependent (the gather of this layer-step) launch its CTAs now; they
     // wait for this grid's completion before reading its outputs.
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kBigThreads, 1) sieve_big_kernel(const SievePa
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const uint32_t mask = static_cast<uint32_t>(p.ht_size) - 1u;
     const BigLayout L = big_layout(p.ht_size, p.vis_stride, K, dbs);
-    const BigSlot G = big_slot(dbs, padded);
+    const BigSlot G = big_slot(dbs, padded, K);
     unsigned char *gs = p.big + static_cast<size_t>(blockIdx.x) * p.big_slot_bytes;
     uint16_t *g_idx = reinterpret_cast<uint16_t *>(gs + G.idx);
     uint32_t *tf = reinterpret_cast<uint32_t *>(gs + G.tf);  // (Tl << 16) | Tf per hot slot
@@ -199,14 +203,14 @@ __global__ void __launch_bounds__(kBigThreads, 1) sieve_big_kernel(const SievePa
     uint16_t *s_aux = reinterpret_cast<uint16_t *>(smem + L.aux);
     uint32_t *s_missb = reinterpret_cast<uint32_t *>(smem + L.missb);
     uint16_t *s_posl = reinterpret_cast<uint16_t *>(smem + L.posl);
-    int32_t *s_dkey = reinterpret_cast<int32_t *>(smem + L.dkey);
-    int32_t *s_dfirst = reinterpret_cast<int32_t *>(smem + L.dfirst);
-    uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
+    int32_t *s_dkey = reinterpret_cast<int32_t *>(gs + G.dkey);
+    int32_t *s_dfirst = reinterpret_cast<int32_t *>(gs + G.dfirst);
+    uint32_t *s_wofs = reinterpret_cast<uint32_t *>(gs + G.wofs);
     uint32_t *freeb = reinterpret_cast<uint32_t *>(smem + L.freeb);
     uint32_t *delb = reinterpret_cast<uint32_t *>(smem + L.delb);
     int32_t *runs = reinterpret_cast<int32_t *>(smem + L.delb);  // phase 0 view of delb
-    uint32_t *leads = reinterpret_cast<uint32_t *>(smem + L.dkey);  // phase 4 view of dkey
-    const uint32_t dmask = static_cast<uint32_t>(L.dcap) - 1u;
+    uint32_t *leads = reinterpret_cast<uint32_t *>(gs + G.dkey);  // phase 4 view of dkey
+    const uint32_t dmask = static_cast<uint32_t>(G.dcap) - 1u;
     const int32_t fwords = L.fwords;
 
     int32_t num_real = *p.num_real;
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(kBigThreads, 1) sieve_big_kernel(const SievePa
             cellof[i] = kNoCell;
         }
         for (int32_t i = tid; i < padded; i += nt) evt[i] = kNone16;
-        for (int32_t i = tid; i < L.dcap; i += nt) {
+        for (int32_t i = tid; i < G.dcap; i += nt) {
             s_dkey[i] = -1;
             s_dfirst[i] = 0x7FFFFFFF;
         }
