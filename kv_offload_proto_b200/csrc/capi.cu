@@ -48,7 +48,7 @@ struct DeviceState {
     uint2 *wl = nullptr;         // cooperative layer-steps: kWalkListBufs walk-list buffers
     size_t wl_entries = 0;       // entries per buffer
     std::vector<uint2 *> wl_old;  // outgrown buffers (a captured graph may still name one)
-    uint8_t *big = nullptr;      // large-table SIEVE tier: zeroed scratch (the kernel leaves it zero)
+    uint8_t *big = nullptr;      // large-table SIEVE tier: scratch (no initial contents needed)
     size_t big_bytes = 0;
     std::vector<uint8_t *> big_old;  // outgrown scratch (a captured graph may still name one)
 };
@@ -391,7 +391,8 @@ int ensure_walk_lists(DeviceState *ds, size_t entries)
     return KVOPS_OK;
 }
 
-// Grows (once per shape, never shrinking) the large-table tier's scratch to `bytes`, zeroed.
+// Grows (once per shape, never shrinking) the large-table tier's scratch to `bytes` (zeroed for
+// tidiness only: the kernel initialises every array it reads).
 int ensure_big_scratch(DeviceState *ds, size_t bytes)
 {
     std::lock_guard<std::mutex> lk(g_mu);

@@ -165,8 +165,8 @@ int clear_status_words(uint64_t status, uint32_t node_lo, uint32_t node_hi, uint
 void set_sieve_tier(uint32_t tier);
 uint32_t last_sieve_tier();
 // Bytes of one slot of the large-table tier's scratch and the slots it needs (*slots = 0: the
-// shape does not use that tier under the calling thread's choice). The scratch must be zero
-// when first used; the kernel leaves it zero again.
+// shape does not use that tier under the calling thread's choice). The kernel needs no initial
+// contents in it.
 uint64_t sieve_big_scratch(const SieveParams &p, int sm_count, int32_t *slots);
 
 // Kernel launchers (defined next to their kernels).

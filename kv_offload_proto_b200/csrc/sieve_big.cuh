@@ -13,7 +13,8 @@
 //     entry names a hot slot holding a token, each slot has exactly one entry, tokens are
 //     distinct, and every entry is reachable from its home through occupied cells); then
 //     ht_find(t) is, exactly, the slot whose token is t, which a direct token -> slot index
-//     (tokens below kBigIdxCap) answers in one load. A state that fails the check, or holds a
+//     (tokens below kBigIdxCap) answers in one load, checked against the token row (the index
+//     keeps whatever earlier requests left in it). A state that fails the check, or holds a
 //     token the index cannot hold, runs the position-ordered loop in global memory instead;
 //  1-3. the phases of sieve_fast_kernel (probe classification, hand sweep, outputs) with the
 //     index in place of the probes and the per-slot arrays in global scratch;
@@ -59,7 +60,7 @@ __host__ __device__ __forceinline__ BigLayout big_layout(int32_t ht_size, int32_
     return L;
 }
 
-// Global scratch of one CTA: the token index (zero between requests), the per-slot arrays, the
+// Global scratch of one CTA: the token index (no initial contents needed), the per-slot arrays, the
 // de-duplication table of phase 1 (then the list of run leads of phase 4) and the word offsets
 // of the candidate list.
 struct BigSlot {
@@ -298,15 +299,26 @@ __global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SievePa
         if (__syncthreads_or(bad)) {
             if (tid == 0) s_flag = 1;
         } else {
+            // The index: every token's slot (the index may hold anything beforehand; every
+            // lookup below checks the slot it reads against the token row).
             for (int32_t s = tid; s < dbs && !bad; s += nt) {
                 const int32_t t = g_tok[s];
                 if (t < 0) continue;
-                if (t >= kBigIdxCap || cellof[s] == kNoCell ||
-                    atomicCAS(reinterpret_cast<unsigned short *>(&g_idx[t]), static_cast<unsigned short>(0),
-                              static_cast<unsigned short>(s + 1)) != 0)
+                if (t >= kBigIdxCap || cellof[s] == kNoCell) {
                     bad = true;
+                    break;
+                }
+                g_idx[t] = static_cast<uint16_t>(s + 1);
             }
-            if (__syncthreads_or(bad) && tid == 0) s_flag = 1;
+            if (__syncthreads_or(bad)) {
+                if (tid == 0) s_flag = 1;
+            } else {
+                for (int32_t s = tid; s < dbs && !bad; s += nt) {  // a token held by two slots: one store lost
+                    const int32_t t = g_tok[s];
+                    if (t >= 0 && g_idx[t] != static_cast<uint16_t>(s + 1)) bad = true;
+                }
+                if (__syncthreads_or(bad) && tid == 0) s_flag = 1;
+            }
         }
         __syncthreads();
 
@@ -325,7 +337,9 @@ __global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SievePa
                     s_om[k] = 0;
                     continue;
                 }
-                const int32_t s0 = t < kBigIdxCap ? static_cast<int32_t>(g_idx[t]) - 1 : -1;
+                // resident iff the index names a hot slot that holds t (tokens are distinct)
+                int32_t s0 = t < kBigIdxCap ? static_cast<int32_t>(g_idx[t]) - 1 : -1;
+                if (s0 >= dbs || (s0 >= 0 && g_tok[s0] != t)) s0 = -1;
                 if (s0 >= 0) {
                     s_cls[k] = kClsRes;
                     s_aux[k] = static_cast<uint16_t>(s0);
@@ -442,12 +456,7 @@ __global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SievePa
                 }
             }
             __syncthreads();
-            // ---- phase 6: clear the index (initial tokens), write back ----
-            for (int32_t s = tid; s < dbs; s += nt) {
-                const int32_t t = g_tok[s];
-                if (t >= 0 && t < kBigIdxCap) g_idx[t] = 0;
-            }
-            __syncthreads();
+            // ---- phase 6: write back ----
             for (int32_t m = tid; m < K; m += nt)
                 if ((s_missb[m >> 5] >> (m & 31)) & 1u) g_tok[s_os[m]] = s_topk[m];
             coop_copy(g_vis, vfin, static_cast<size_t>(p.vis_stride));
@@ -456,11 +465,6 @@ __global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SievePa
         }
 
         // ---- the position-ordered loop in global memory (a state the check refuses, a wrapped sweep) ----
-        for (int32_t s = tid; s < dbs; s += nt) {
-            const int32_t t = g_tok[s];
-            if (t >= 0 && t < kBigIdxCap) g_idx[t] = 0;
-        }
-        __syncthreads();
         if (tid == 0) {
             int32_t hand = *g_hand;
             if (hand < 0 || hand >= dbs) hand = 0;
