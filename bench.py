@@ -455,6 +455,7 @@ def run_decode(args, cfg):
         cl.barrier()
         torch.cuda.nvtx.range_push("timed" if graphs or args.no_graph else "per_call")  # profiler selection
         t0.record()
+        h0 = time.perf_counter()
         for s in range(W, T):
             if graphs:
                 e = evs[s - W]
@@ -468,10 +469,12 @@ def run_decode(args, cfg):
                 layer_step(s, l)
                 e[1].record()
         t1.record()
+        host_issue_s = time.perf_counter() - h0
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         cl.barrier()
         clk = clocks.stop()
+        clk["host_issue_us_per_call"] = host_issue_s * 1e6 / (Sn * (1 if graphs else L))
         assert int(co.is_miss.sum().item()) == int(misses_h[T - 1, L - 1]), "replay diverged from the input pass"
         return t0.elapsed_time(t1) * 1e-3, [e[0].elapsed_time(e[1]) * 1e3 for e in evs], clk
 
@@ -808,6 +811,7 @@ def report_decode(args, cfg, world, gathered, co, L, n_nodes, injective):
         "per_call": {"value": miss_rows * ROW_BYTES / max(g["per_call"]["ms_per_step"] for g in gathered) /
                      args.steps / 1e6, "unit": "GB/s",
                      "ms_per_step": max(g["per_call"]["ms_per_step"] for g in gathered),
+                     "host_issue_us_per_call": g0["per_call"]["clocks"].get("host_issue_us_per_call"),
                      "note": "one sieve_and_read call per layer with status words, CUDA events around each call"},
         "per_rank": [{"rank": g["rank"], "ms_per_step": g["elapsed"] * 1e3 / args.steps,
                       "us_per_layer_step": g["elapsed"] * 1e6 / (args.steps * L), "miss_rows": g["miss_rows"],
