@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--verify-rows", type=int, default=4096, help="gathered rows byte-checked per rank")
+    ap.add_argument("--link-span-gb", type=int, default=2,
+                    help="link: also draw the all-GPU random reads from segments of this many GB (> 2)")
     return ap.parse_args()
 
 
@@ -1205,22 +1207,37 @@ def run_link(args):
         out["one_peer_random_per_gpu"] = all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=True)
         for a in segs:
             mod.segment_free(a)
+        if args.link_span_gb > 2:  # the same reads drawn from segments of the decode pool's size
+            span = args.link_span_gb << 30
+            segs = [mod.segment_alloc(g, span) for g in range(ngpu)]
+            out["span_gb"] = args.link_span_gb
+            out["all_peers_random_per_gpu_span"] = all_to_all(torch, mod, segs, ngpu, nrows, reps,
+                                                              seg_rows=span // ROW_BYTES)
+            out["one_peer_random_per_gpu_span"] = all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=True,
+                                                             seg_rows=span // ROW_BYTES)
+            out["own_random_span"] = all_to_all(torch, mod, segs, 1, nrows, reps, own=True,
+                                                seg_rows=span // ROW_BYTES)
+            for a in segs:
+                mod.segment_free(a)
     print(json.dumps(out), flush=True)
 
 
-def all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=False, K=4096):
+def all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=False, K=4096, seg_rows=None, own=False):
     """Every GPU at once gathers nrows random rows from other GPUs' segments: from all of them
-    (striped, the pool layout of config 2) or, with one_peer, only from GPU (g + 1) % N. One
-    launch per GPU per repetition; returns per-GPU GB/s."""
+    (striped, the pool layout of config 2) or, with one_peer, only from GPU (g + 1) % N; with own,
+    from its own segment. Rows are drawn from the first seg_rows rows of each segment (default
+    nrows / segments). One launch per GPU per repetition; returns per-GPU GB/s."""
     per = []
     setup = []
     for g in range(ngpu):
         with torch.cuda.device(g):
-            others = [segs[(g + 1) % ngpu]] if one_peer else [segs[h] for h in range(ngpu) if h != g]
+            others = [segs[g]] if own else [segs[(g + 1) % len(segs)]] if one_peer else \
+                [segs[h] for h in range(len(segs)) if h != g]
             n = len(others)
             R = (nrows + K - 1) // K
+            span = seg_rows if seg_rows else nrows // n
             gen = torch.Generator(device="cuda").manual_seed(g + 11)
-            rows = torch.randint(0, (nrows // n) * n, (R * K,), generator=gen, device="cuda", dtype=torch.int64)
+            rows = torch.randint(0, span * n, (R * K,), generator=gen, device="cuda", dtype=torch.int64)
             topk = rows.to(torch.int32).view(R, K)
             slots = (torch.arange(R * K, dtype=torch.int32, device="cuda") % K).view(R, K)
             miss = torch.ones((R, K), dtype=torch.int8, device="cuda")
@@ -1229,20 +1246,20 @@ def all_to_all(torch, mod, segs, ngpu, nrows, reps, one_peer=False, K=4096):
             nr = torch.tensor([R], dtype=torch.int32, device="cuda")
             hot = torch.empty(R * K * ROW_BYTES, dtype=torch.uint8, device="cuda")
             st = torch.cuda.Stream()
-            setup.append((others, topk, slots, miss, pool_idx, base, nr, hot, st, R))
+            setup.append((others, topk, slots, miss, pool_idx, base, nr, hot, st, R, span))
     evs = []
     for g in range(ngpu):
         with torch.cuda.device(g):
             evs.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
     for phase in range(2):  # warm-up, then timed
         for g in range(ngpu):
-            others, topk, slots, miss, pool_idx, base, nr, hot, st, R = setup[g]
+            others, topk, slots, miss, pool_idx, base, nr, hot, st, R, span = setup[g]
             with torch.cuda.device(g):
                 with torch.cuda.stream(st):
                     if phase:
                         evs[g][0].record(st)
                     for _ in range(reps if phase else 1):
-                        mod.import_multi(others, 0, nrows // len(others), ROW_BYTES, topk.data_ptr(),
+                        mod.import_multi(others, 0, span, ROW_BYTES, topk.data_ptr(),
                                          pool_idx.data_ptr(), base.data_ptr(), slots.data_ptr(), miss.data_ptr(),
                                          nr.data_ptr(), hot.data_ptr(), K, R, 1, 0, st.cuda_stream, 1,
                                          hot_req_stride_rows=K)
