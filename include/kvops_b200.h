@@ -269,7 +269,9 @@ int kvops_import_multi_noalloc(uint32_t node_num, const uint64_t *seg_bases, uin
 
 /* Pool plumbing that replaces the EMS control plane (not a reference entry point):
  * segment memory on a device (or pinned host memory with device = -1), peer access,
- * and CUDA IPC so that one process per GPU can map the other GPUs' segments. */
+ * and CUDA IPC so that one process per GPU can map the other GPUs' segments. Device
+ * segments are allocated in whole 2 MiB units (other GPUs read an IPC-mapped allocation of
+ * any other size at under half the NVLink rate). */
 int kvops_segment_alloc(int device, uint64_t bytes, uint64_t *out_addr);
 int kvops_segment_free(uint64_t addr);
 int kvops_enable_peer_access(int device, int peer);

@@ -858,6 +858,13 @@ int kvops_segment_alloc(int device, uint64_t bytes, uint64_t *out_addr)
         cudaError_t e = cudaHostAlloc(&p, bytes, cudaHostAllocMapped | cudaHostAllocPortable);
         if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(segment)");
     } else {
+        // Device segments are allocated in whole 2 MiB units. A segment is read by other GPUs
+        // through CUDA IPC, and an allocation whose size is not a multiple of 2 MiB was mapped
+        // there so that random row reads crossing many pages ran at under half the link rate
+        // (N=4 B200, 61 per-layer regions of 201 MB: 251 GB/s per GPU against 540 GB/s with the
+        // size rounded up); local reads are unaffected.
+        constexpr uint64_t kUnit = 2ull << 20;
+        bytes = (bytes + kUnit - 1) / kUnit * kUnit;
         int cur = 0;
         cudaGetDevice(&cur);
         cudaError_t e = cudaSetDevice(device);
