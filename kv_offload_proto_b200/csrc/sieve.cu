@@ -1471,17 +1471,28 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     }
     __syncthreads();
     if (!s_flag) {
-        for (int32_t k = tid; k < K; k += nt) {
-            if (s_cls[k] != kClsNew) continue;
-            const int32_t t = s_topk[k];
-            uint32_t d = ht_hash(t) & dmask;
-            for (uint32_t n = 0; n <= dmask && s_dkey[d] != t; ++n) d = (d + 1) & dmask;
-            const int32_t f = s_dfirst[d];
-            s_aux[k] = static_cast<uint16_t>(f);
-            if (f == k) atomicOr(&s_missb[k >> 5], 1u << (k & 31));  // first lookup of a new token
+        // A warp covers 32 consecutive positions (slots), one bitmap word, per iteration: the
+        // word's bits are gathered by ballot and stored by one lane (no atomics on a shared word).
+        const int lane = tid & 31;
+        for (int32_t kb = tid - lane; kb < K; kb += nt) {
+            const int32_t k = kb + lane;
+            bool first = false;
+            if (k < K && s_cls[k] == kClsNew) {
+                const int32_t t = s_topk[k];
+                uint32_t d = ht_hash(t) & dmask;
+                for (uint32_t n = 0; n <= dmask && s_dkey[d] != t; ++n) d = (d + 1) & dmask;
+                const int32_t f = s_dfirst[d];
+                s_aux[k] = static_cast<uint16_t>(f);
+                first = f == k;  // first lookup of a new token
+            }
+            const uint32_t b = __ballot_sync(0xFFFFFFFFu, first);
+            if (lane == 0 && b != 0u) s_missb[kb >> 5] |= b;
         }
-        for (int32_t c = tid; c < dbs; c += nt)  // default final bit: initial bit, or a hit this step
-            if ((s_tf[c] & 0xFFFFu) != kNone16) atomicOr(&s_vfin[c >> 5], 1u << (c & 31));
+        for (int32_t cb = tid - lane; cb < dbs; cb += nt) {  // default final bit: initial bit, or a hit
+            const int32_t c = cb + lane;
+            const uint32_t b = __ballot_sync(0xFFFFFFFFu, c < dbs && (s_tf[c] & 0xFFFFu) != kNone16);
+            if (lane == 0 && b != 0u) s_vfin[cb >> 5] |= b;
+        }
     }
     __syncthreads();
 
