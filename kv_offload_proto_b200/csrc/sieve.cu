@@ -1001,12 +1001,15 @@ __device__ int32_t list_misses_in_order(const StepExtra &x, const int8_t *om, co
 // prog[0] are final (a miss the walk creates always follows every miss consumed before it),
 // each number's position being that set bit of the miss queue. Entry m of request bid's walk
 // list is {token, (position << 16) | slot}; after each batch the count is published
-// (wl_publish). Listing stops when the walk has ended (prog[1]). Returns (in warp 1) how many
-// numbers were listed: exactly the misses at positions below the position of that number.
+// (wl_publish). When the walk has ended (prog[1]: 1 = completed, 2 = failed), a completed walk's
+// remaining numbers are listed and the list is published as final at once (*final_out = 1):
+// with every candidate verified the outputs are final when the walk completes. Returns (in warp
+// 1) how many numbers were listed: exactly the misses at positions below the position of that
+// number.
 __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n, const int32_t *tok,
                              const uint16_t *ht, uint32_t mask, int32_t padded, const int32_t *topk,
                              const uint32_t *missb, const uint16_t *nslot, const int32_t *prog, int32_t K, int32_t bid,
-                             uint16_t *hpos, int *verified)
+                             uint16_t *hpos, int *verified, int *final_out)
 {
     const unsigned kAll = 0xFFFFFFFFu;
     const int htid = helper_index(threadIdx.x), lane = threadIdx.x & 31;
@@ -1051,10 +1054,19 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
         }
         done = __shfl_sync(kAll, done, 0);
         gm = __shfl_sync(kAll, gm, 0);
-        if (done) break;
+        if (done == 2) break;  // the walk failed: the step falls back and relists everything
         const int32_t m1 = min(gm, m0 + kHelpBatch);
-        if (m1 <= m0) {  // nothing new yet
-            __nanosleep(128);
+        if (m1 <= m0) {
+            if (done) {  // every number is listed: the list is final
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    wl_publish(x, bid, m0, true);
+                    *final_out = 1;
+                }
+                break;
+            }
+            __nanosleep(128);  // nothing new yet
             continue;
         }
         __threadfence_block();
@@ -1091,9 +1103,8 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
             wl[m0 + j] = make_uint2(static_cast<uint32_t>(topk[pos]), (pos << 16) | nslot[m0 + j]);
         }
         m0 = m1;
-        // If the walk has ended meanwhile, the final publish (after the CTA's barrier and fence)
-        // covers this batch: skip the fence, which the CTA would wait for.
-        if (__shfl_sync(kAll, lane == 0 ? vprog[1] : 0, 0) != 0) break;
+        // Once the walk has ended the next pass lists the rest and publishes the list as final.
+        if (done || __shfl_sync(kAll, lane == 0 ? vprog[1] : 0, 0) != 0) continue;
         __threadfence();
         __syncwarp();
         if (lane == 0) wl_publish(x, bid, m1, false);
@@ -1343,6 +1354,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __shared__ int32_t s_prog[2];  // cooperative step: misses the walk has consumed; walk ended
     __shared__ int32_t s_hm;           // walk list: numbers listed during the walk
     __shared__ int s_hver;             // every candidate's table entry checked (phase 3 need not)
+    __shared__ int s_hfinal;           // the helper published the walk list as final
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -1419,6 +1431,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         s_prog[0] = s_prog[1] = 0;
         s_hm = 0;
         s_hver = 0;
+        s_hfinal = 0;
         s_ndel = 0;
     }
     cp_async_wait_all();
@@ -1518,7 +1531,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
                                         kMode == 2 ? s_prog : nullptr);
         if (kMode == 2 && tid == 0) {  // the walk has ended: the helpers stop after their batch
             __threadfence_block();
-            reinterpret_cast<volatile int32_t *>(s_prog)[1] = 1;
+            reinterpret_cast<volatile int32_t *>(s_prog)[1] = ok ? 1 : 2;
         }
         if (tid == 0) {
             if (!ok) s_flag = 1;
@@ -1533,7 +1546,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         if (is_walk_helper(tid)) {
             const int32_t hm = help_walk(x, s_cand, s_ncand, s_tok, s_ht, mask, padded, s_topk, s_missb,
                                          reinterpret_cast<const uint16_t *>(smem + L.nslot), s_prog, K, bid,
-                                         reinterpret_cast<uint16_t *>(smem + L.hpos), &s_hver);
+                                         reinterpret_cast<uint16_t *>(smem + L.hpos), &s_hver, &s_hfinal);
             if (tid == 32) s_hm = hm;
         }
     }
@@ -1619,7 +1632,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
             }
         }
         sync();
-        if (t == 0) {
+        if (t == 0 && !s_hfinal) {  // else the helper published every entry as final already
             __threadfence();  // the walk list's entries and the outputs above
             wl_publish(x, bid, x.wl != nullptr ? gm : 0, true);
         }
