@@ -1112,19 +1112,29 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
     return m0;
 }
 
-constexpr int kCopyChunk = 256;  // walk-list entries per chunk when a request's list is shared
+constexpr int kCopyChunk = 64;  // walk-list entries per chunk when a request's list is shared
+
+// Shares per request list: about four units per copy CTA (a CTA holds at most 32, one per lane
+// of its polling warp), one when the copy CTAs number fewer than half the requests.
+__device__ __forceinline__ int32_t copy_shares(int32_t ncopy, int32_t nr)
+{
+    if (2 * ncopy < nr) return 1;
+    const int32_t want = (4 * ncopy + nr - 1) / nr, cap = (32 * ncopy) / nr;
+    return max(1, min(want, cap));
+}
 
 // Copy CTA cidx of ncopy during the walks. The work is cut into units u = j * nr + r: share j of
-// request r's walk list, nb shares per request (nb = ncopy / nr when there are at least two copy
-// CTAs per request, else 1). Share j holds the list's chunks of kCopyChunk entries j, j + nb, ...
-// (all of it when nb = 1), so the shares stay even whatever the list's final length. CTA cidx
-// holds units cidx, cidx + ncopy, ... (at most 32: nr <= 252 and ncopy >= 8); lane i of warp 0
-// polls the list of the i-th, and each round the CTA copies the published entries of the unit
-// with the most waiting (up to one per thread), until every unit it holds is final and copied.
+// request r's walk list, nb = copy_shares(ncopy, nr) shares per request. Share j holds the
+// list's chunks of kCopyChunk entries j, j + nb, ... (all of it when nb = 1), so the shares stay
+// even whatever the list's final length. CTA cidx holds units cidx, cidx + ncopy, ... (at most
+// 32); lane i of warp 0 polls the list of the i-th. Each round the CTA copies the published
+// entries of every unit it holds, up to one entry per thread (the lanes' waiting counts are
+// scanned into one flat list of rows), until every unit is final and copied.
 __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsigned char *smem, int32_t nr,
                                 int32_t K, int32_t cidx, int32_t ncopy)
 {
-    __shared__ int32_t s_r, s_t0, s_t1;
+    __shared__ int32_t s_ur[32], s_ut0[32], s_ubase[32];
+    __shared__ int32_t s_total;
     __shared__ int s_wn, s_last;
     const unsigned kAll = 0xFFFFFFFFu;
     const unsigned tid = threadIdx.x, nt = blockDim.x;
@@ -1132,7 +1142,7 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
     const uint8_t **srcl = reinterpret_cast<const uint8_t **>(smem);
     uint8_t **dstl = reinterpret_cast<uint8_t **>(smem + 8 * nt);
     if (nr <= 0 || K <= 0) return;
-    const int32_t nb = ncopy >= 2 * nr ? ncopy / nr : 1;
+    const int32_t nb = copy_shares(ncopy, nr);
     const int32_t chunk = nb > 1 ? kCopyChunk : K;  // nb = 1: the whole list is one chunk
     const int64_t nunits = static_cast<int64_t>(nb) * nr;
     const int64_t u = static_cast<int64_t>(cidx) + static_cast<int64_t>(lane) * ncopy;  // lane's unit (warp 0)
@@ -1150,43 +1160,52 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
                 const int32_t pv = wl_probe(x, r);
                 cnt = pv < 0 ? 0 : (pv >> 1);
                 fin = pv >= 0 && (pv & 1) != 0;
-                avail = min(cnt, (ck + 1) * chunk) - mine;
+                avail = max(min(cnt, (ck + 1) * chunk) - mine, 0);
                 if (fin && mine >= cnt) done_lane = true;
             }
-            const int32_t best = static_cast<int32_t>(__reduce_max_sync(kAll, static_cast<uint32_t>(max(avail, 0))));
-            if (best > 0) {
-                const int pick = __ffs(__ballot_sync(kAll, avail == best)) - 1;
-                if (lane == pick) {
-                    s_r = r;
-                    s_t0 = mine;
-                    s_t1 = mine + min(best, static_cast<int32_t>(nt));
-                    mine = s_t1;
-                    if (mine >= (ck + 1) * chunk) {  // chunk done: the share's next one
-                        ck += nb;
-                        mine = ck * chunk;
-                    }
-                    if (fin && mine >= cnt) done_lane = true;  // this chunk ends a final unit
-                }
+            int32_t incl = avail;  // the lanes' waiting entries, scanned in lane order
+            for (int d = 1; d < 32; d <<= 1) {
+                const int32_t v = __shfl_up_sync(kAll, incl, d);
+                if (lane >= d) incl += v;
             }
-            // Every unit done once this chunk (if any) is copied: no further poll is needed.
+            const int32_t excl = incl - avail;
+            const int32_t take = max(0, min(avail, static_cast<int32_t>(nt) - excl));
+            s_ur[lane] = r;
+            s_ut0[lane] = mine;
+            s_ubase[lane] = excl;
+            if (take > 0) {
+                mine += take;
+                if (mine >= (ck + 1) * chunk) {  // chunk done: the share's next one
+                    ck += nb;
+                    mine = ck * chunk;
+                }
+                if (fin && mine >= cnt) done_lane = true;  // this round ends a final unit
+            }
+            // Every unit done once this round's rows (if any) are copied: no further poll.
             const bool all_done = __ballot_sync(kAll, done_lane) == kAll;
+            const int32_t total = min(__shfl_sync(kAll, incl, 31), static_cast<int32_t>(nt));
             if (lane == 0) {
-                if (best == 0) s_r = all_done ? -2 : -1;
-                s_last = best > 0 && all_done ? 1 : 0;
+                s_total = total;
+                s_last = all_done ? 1 : 0;
             }
         }
         __syncthreads();
-        const int32_t rr = s_r;
-        if (rr == -2) {
-            finished = true;
-        } else if (rr >= 0) {
-            if (s_last) finished = true;  // after this copy
-            const int32_t t0 = s_t0, t1 = s_t1;
+        const int32_t total = s_total;
+        if (s_last) finished = true;  // after this round's copy
+        if (total > 0) {
             const uint8_t *src = nullptr;
             uint8_t *dst = nullptr;
             bool ok = false;
-            if (t0 + static_cast<int32_t>(tid) < t1) {
-                const uint2 e = __ldcg(x.wl + static_cast<int64_t>(rr) * K + t0 + tid);
+            if (static_cast<int32_t>(tid) < total) {
+                // the lane whose entries hold flat index tid: the last with base <= tid (bases
+                // are the exclusive scan, so any later lane starts past tid)
+                int L = 0;
+#pragma unroll
+                for (int step = 16; step >= 1; step >>= 1)
+                    if (s_ubase[L + step] <= static_cast<int32_t>(tid)) L += step;
+                const int32_t rr = s_ur[L];
+                const int32_t e_at = s_ut0[L] + static_cast<int32_t>(tid) - s_ubase[L];
+                const uint2 e = __ldcg(x.wl + static_cast<int64_t>(rr) * K + e_at);
                 const int32_t pos = static_cast<int32_t>(e.y >> 16), slot = static_cast<int32_t>(e.y & 0xFFFFu);
                 ok = gather_eval(g, static_cast<int64_t>(rr) * K + pos, 1, static_cast<int32_t>(e.x), slot,
                                  g.req_pool[rr], g.host_base[rr], &src, &dst);
@@ -1194,7 +1213,7 @@ __device__ void copy_walk_lists(const GatherParams &g, const StepExtra &x, unsig
             list_append(ok, src, dst, srcl, dstl, &s_wn);
             __syncthreads();
             cta_copy_rows<uint4, kCoopUnroll>(srcl, dstl, s_wn, g.row_bytes, x.magic);
-        } else {
+        } else if (!finished) {
             __nanosleep(256);
         }
         __syncthreads();
