@@ -1678,8 +1678,9 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
 
     // ---- phase 5: insert the new tokens; an earlier miss wins a contested cell ----
     // One pass per round: a placed key first checks that it still owns its cell (a displaced
-    // one moves on), a pending key then tries its current cell. The round's barrier ORs the
-    // progress flags; a round without a pending or displaced key leaves the table final.
+    // one moves on), a pending key then passes the cells closed to it and claims the next. The
+    // round's barrier ORs the progress flags; a round without a pending or displaced key leaves
+    // the table final.
     if (update_table) {
         for (int32_t j = tid; j < nkeys; j += ntc) {  // every miss starts at its token's home cell
             const int32_t m = posl[j];
@@ -1701,19 +1702,19 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
                 }
                 if (cls != kClsPending) continue;
                 ch = true;
-                const uint16_t e = s_ht[at];
-                if (e == kHtEmpty) {
-                    if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), kHtEmpty, entry) == kHtEmpty)
-                        cls = kClsPlaced;
-                } else {
+                // A cell held by a surviving key, or by an earlier miss, stays closed to this key
+                // (an earlier miss is only ever displaced by a still earlier one, and no cell is
+                // emptied here): all such cells are passed in this round.
+                uint16_t e = s_ht[at];
+                for (uint32_t q = 0; q <= mask && e != kHtEmpty; ++q) {
                     const int32_t es = static_cast<int32_t>(e) - 1;
                     const uint16_t te = es < padded ? s_evt[es] : kNone16;
-                    if (te == kNone16 || te < m) {
-                        at = (at + 1) & mask;
-                    } else if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), e, entry) == e) {
-                        cls = kClsPlaced;  // the later miss it displaced moves on
-                    }
+                    if (te != kNone16 && te > m) break;  // a later miss: this key displaces it
+                    at = (at + 1) & mask;
+                    e = s_ht[at];
                 }
+                if (atomicCAS(reinterpret_cast<unsigned short *>(&s_ht[at]), e, entry) == e)
+                    cls = kClsPlaced;  // an empty cell, or a later miss that now moves on
                 s_cls[m] = cls;
                 s_aux[m] = static_cast<uint16_t>(at);
             }
