@@ -412,21 +412,25 @@ __host__ __device__ __forceinline__ FastLayout fast_layout(int32_t padded, int32
 //      others were cleared on arrival and are set again iff their token is looked up after
 //      it. A passed slot's arrival time is that of the next candidate at or after it.
 
-// 2a: candidate list and per-word offsets; returns the candidate count (in *n_out).
-__device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint32_t *cand, uint32_t *wofs,
-                                 int32_t dbs, int32_t *n_out, int32_t *warp_sums)
+// 2a: candidate list and per-word offsets. The offsets depend only on the step-initial bits
+// (candidate_offsets: per word of slots, how many candidates precede it; *n_out the count, set
+// by warp 0; no trailing barrier), the entries also on Tf (put_candidate, one slot).
+__device__ __forceinline__ uint32_t candidate_bits(const uint32_t *vini, int32_t w, int32_t dbs)
+{
+    const int32_t rem = dbs - (w << 5);
+    const uint32_t valid = rem >= 32 ? 0xFFFFFFFFu : ((1u << rem) - 1u);
+    return ~vini[w] & valid;
+}
+
+__device__ void candidate_offsets(const uint32_t *vini, uint32_t *wofs, int32_t dbs, int32_t *n_out,
+                                  int32_t *warp_sums)
 {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
     const int32_t nwords = (dbs + 31) >> 5;
     const int32_t per = (nwords + nt - 1) / nt;
     const int32_t w0 = min(tid * per, nwords), w1 = min(w0 + per, nwords);
-    auto bits_of = [&](int32_t w) -> uint32_t {
-        const int32_t rem = dbs - (w << 5);
-        const uint32_t valid = rem >= 32 ? 0xFFFFFFFFu : ((1u << rem) - 1u);
-        return ~vini[w] & valid;
-    };
     int32_t mine = 0;
-    for (int32_t w = w0; w < w1; ++w) mine += __popc(bits_of(w));
+    for (int32_t w = w0; w < w1; ++w) mine += __popc(candidate_bits(vini, w, dbs));
     // block-wide exclusive scan of `mine`
     int32_t incl = mine;
     for (int d = 1; d < 32; d <<= 1) {
@@ -449,14 +453,24 @@ __device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint3
     int32_t at = warp_sums[wid] + incl - mine;
     for (int32_t w = w0; w < w1; ++w) {
         wofs[w] = static_cast<uint32_t>(at);
-        at += __popc(bits_of(w));
+        at += __popc(candidate_bits(vini, w, dbs));
     }
+}
+
+// Slot c's entry (Tf << 16) | c at its word's offset + the candidates before it, if c is one.
+__device__ __forceinline__ void put_candidate(const uint32_t *vini, const uint32_t *tf, uint32_t *cand,
+                                              const uint32_t *wofs, int32_t dbs, int32_t c)
+{
+    const uint32_t b = candidate_bits(vini, c >> 5, dbs), below = b & ((1u << (c & 31)) - 1u);
+    if ((b >> (c & 31)) & 1u) cand[wofs[c >> 5] + __popc(below)] = ((tf[c] & 0xFFFFu) << 16) | static_cast<uint32_t>(c);
+}
+
+__device__ void build_candidates(const uint32_t *vini, const uint32_t *tf, uint32_t *cand, uint32_t *wofs,
+                                 int32_t dbs, int32_t *n_out, int32_t *warp_sums)
+{
+    candidate_offsets(vini, wofs, dbs, n_out, warp_sums);
     __syncthreads();
-    for (int32_t c = tid; c < dbs; c += nt) {  // one slot per thread: its word's offset + candidates before it
-        const uint32_t b = bits_of(c >> 5), below = b & ((1u << (c & 31)) - 1u);
-        if ((b >> (c & 31)) & 1u)
-            cand[wofs[c >> 5] + __popc(below)] = ((tf[c] & 0xFFFFu) << 16) | static_cast<uint32_t>(c);
-    }
+    for (int32_t c = threadIdx.x; c < dbs; c += blockDim.x) put_candidate(vini, tf, cand, wofs, dbs, c);
 }
 
 // 2b: the walk (one warp), 32 candidates per batch, one per lane, in sweep order from the
@@ -1374,6 +1388,7 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
     __shared__ int32_t s_hm;           // walk list: numbers listed during the walk
     __shared__ int s_hver;             // every candidate's table entry checked (phase 3 need not)
     __shared__ int s_hfinal;           // the helper published the walk list as final
+    __shared__ int s_dup;              // a new token is looked up more than once
     const int32_t bid = blockIdx.x;
     const int32_t K = p.top_k, dbs = p.dbs, padded = p.padded;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -1451,31 +1466,40 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         s_hm = 0;
         s_hver = 0;
         s_hfinal = 0;
+        s_dup = 0;
         s_ndel = 0;
     }
     cp_async_wait_all();
     __syncthreads();
     if (kMode == 2) x.epoch = s_epoch;
 
+    // The candidate list's offsets need only the step-initial bits: computed before phase 1.
+    uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
+    candidate_offsets(s_vini, s_wofs, dbs, &s_ncand, s_warp);
+
     // ---- phase 1: classify and probe every position against the step-initial table ----
-    for (int32_t k = tid; k < K; k += nt) {
+    // A warp covers 32 consecutive positions, one miss-queue word, per iteration. A new token's
+    // position is taken as its first lookup (the word's bits by ballot); a repeated new token
+    // (seen in the de-duplication table) makes the second pass below recompute them.
+    const int lane = tid & 31;
+    auto classify = [&](int32_t k) -> bool {  // true: k looks up a token not in the table
         const int32_t t = s_topk[k];
         s_cls[k] = kClsNone;
         if (t < 0 || t >= seq_len) {
             s_os[k] = -1;
             s_om[k] = 0;
-            continue;
+            return false;
         }
         if (t >= prefill) {
             s_os[k] = padded + (t - prefill);
             s_om[k] = 0;
-            continue;
+            return false;
         }
         const int32_t s0 = ht_find(s_ht, s_tok, t, mask, padded);
         if (s0 >= 0) {
             if (s0 >= dbs) {  // a table entry outside the hot slots: not a state these kernels build
                 s_flag = 1;
-                continue;
+                return false;
             }
             s_cls[k] = kClsRes;
             s_aux[k] = static_cast<uint16_t>(s0);
@@ -1488,51 +1512,59 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
                 if (nw == assumed) break;
                 old = atomicCAS(&s_tf[s0], assumed, nw);
             } while (old != assumed);
-        } else {
-            s_cls[k] = kClsNew;
-            uint32_t d = ht_hash(t) & dmask;
-            for (uint32_t n = 0; n <= dmask; ++n) {
-                const int32_t prev = atomicCAS(&s_dkey[d], -1, t);
-                if (prev == -1 || prev == t) {
-                    atomicMin(&s_dfirst[d], k);
-                    break;
-                }
-                d = (d + 1) & dmask;
-            }
+            return false;
         }
+        s_cls[k] = kClsNew;
+        s_aux[k] = static_cast<uint16_t>(k);
+        uint32_t d = ht_hash(t) & dmask;
+        for (uint32_t n = 0; n <= dmask; ++n) {
+            const int32_t prev = atomicCAS(&s_dkey[d], -1, t);
+            if (prev == -1 || prev == t) {
+                if (prev == t) s_dup = 1;
+                atomicMin(&s_dfirst[d], k);
+                break;
+            }
+            d = (d + 1) & dmask;
+        }
+        return true;
+    };
+    for (int32_t kb = tid - lane; kb < K; kb += nt) {
+        const bool fresh = kb + lane < K && classify(kb + lane);
+        const uint32_t b = __ballot_sync(0xFFFFFFFFu, fresh);
+        if (lane == 0) s_missb[kb >> 5] = b;
     }
     __syncthreads();
+    uint32_t *s_cand = reinterpret_cast<uint32_t *>(smem + L.dkey);  // shares the dedup table's space
     if (!s_flag) {
-        // A warp covers 32 consecutive positions (slots), one bitmap word, per iteration: the
-        // word's bits are gathered by ballot and stored by one lane (no atomics on a shared word).
-        const int lane = tid & 31;
-        for (int32_t kb = tid - lane; kb < K; kb += nt) {
-            const int32_t k = kb + lane;
-            bool first = false;
-            if (k < K && s_cls[k] == kClsNew) {
-                const int32_t t = s_topk[k];
-                uint32_t d = ht_hash(t) & dmask;
-                for (uint32_t n = 0; n <= dmask && s_dkey[d] != t; ++n) d = (d + 1) & dmask;
-                const int32_t f = s_dfirst[d];
-                s_aux[k] = static_cast<uint16_t>(f);
-                first = f == k;  // first lookup of a new token
+        if (s_dup) {  // a new token looked up twice: only its first lookup is a miss
+            for (int32_t kb = tid - lane; kb < K; kb += nt) {
+                const int32_t k = kb + lane;
+                bool first = false;
+                if (k < K && s_cls[k] == kClsNew) {
+                    const int32_t t = s_topk[k];
+                    uint32_t d = ht_hash(t) & dmask;
+                    for (uint32_t n = 0; n <= dmask && s_dkey[d] != t; ++n) d = (d + 1) & dmask;
+                    const int32_t f = s_dfirst[d];
+                    s_aux[k] = static_cast<uint16_t>(f);
+                    first = f == k;
+                }
+                const uint32_t b = __ballot_sync(0xFFFFFFFFu, first);
+                if (lane == 0) s_missb[kb >> 5] = b;
             }
-            const uint32_t b = __ballot_sync(0xFFFFFFFFu, first);
-            if (lane == 0 && b != 0u) s_missb[kb >> 5] |= b;
+            __syncthreads();  // the de-duplication table is read no more: the candidates may overwrite it
         }
-        for (int32_t cb = tid - lane; cb < dbs; cb += nt) {  // default final bit: initial bit, or a hit
+        // Per slot: the default final bit (initial bit, or a hit this step), by ballot per word,
+        // and the slot's candidate entry (phase 2a).
+        for (int32_t cb = tid - lane; cb < dbs; cb += nt) {
             const int32_t c = cb + lane;
             const uint32_t b = __ballot_sync(0xFFFFFFFFu, c < dbs && (s_tf[c] & 0xFFFFu) != kNone16);
             if (lane == 0 && b != 0u) s_vfin[cb >> 5] |= b;
+            if (c < dbs) put_candidate(s_vini, s_tf, s_cand, s_wofs, dbs, c);
         }
     }
     __syncthreads();
 
-    // ---- phase 2: the hand sweep (candidate list, warp walk, final bits) ----
-    uint32_t *s_cand = reinterpret_cast<uint32_t *>(smem + L.dkey);  // dedup table no longer needed
-    uint32_t *s_wofs = reinterpret_cast<uint32_t *>(smem + L.wofs);
-    if (!s_flag) build_candidates(s_vini, s_tf, s_cand, s_wofs, dbs, &s_ncand, s_warp);
-    __syncthreads();
+    // ---- phase 2: the hand sweep (walk over the candidate list, final bits) ----
     // Every thread reads the flag before the walk can set it; a barrier separates the two, so
     // all 15 helper warps take the same branch (their named barrier counts all of them).
     const bool walk_step = !s_flag;
