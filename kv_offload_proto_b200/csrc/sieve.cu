@@ -623,14 +623,40 @@ __device__ bool walk_candidates(uint32_t *cand, int32_t n, int32_t n0, uint16_t 
 }
 
 // 2b': miss numbers -> positions. posl[m] = position of the m-th set bit of the miss queue
-// (all threads), then every evicted slot's number and every visited candidate's arrival
-// number is replaced by its position, and the misses' outputs are written. *nmiss: the
-// number of misses.
+// (all threads; known >= 0: posl is complete already and holds `known` numbers), then every
+// evicted slot's number and every visited candidate's arrival number is replaced by its
+// position, and the misses' outputs are written. *nmiss: the number of misses.
+// 2b'': with posl final: every evicted slot's number and every visited candidate's arrival number
+// replaced by its position, and the misses' outputs written.
+__device__ void resolve_outputs(const uint16_t *posl, uint16_t *evt, int32_t *os, int8_t *om, uint32_t *cand,
+                                int32_t n, int32_t n0, int32_t nvis, int32_t dbs)
+{
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int32_t c = tid; c < dbs; c += nt) {
+        const uint16_t m = evt[c];
+        if (m == kNone16) continue;
+        const uint16_t pos = posl[m];
+        evt[c] = pos;
+        os[pos] = c;
+        om[pos] = 1;
+    }
+    for (int32_t sp = tid; sp < nvis; sp += nt) {
+        const int32_t i = n0 + sp >= n ? n0 + sp - n : n0 + sp;
+        const uint32_t x = cand[i];
+        cand[i] = (static_cast<uint32_t>(posl[x >> 16]) << 16) | (x & 0xFFFFu);
+    }
+}
+
 __device__ void resolve_miss_numbers(const uint32_t *missb, int32_t K, uint16_t *posl, uint16_t *evt, int32_t *os,
                                      int8_t *om, uint32_t *cand, int32_t n, int32_t n0, int32_t nvis, int32_t dbs,
-                                     int32_t *warp_sums, int32_t *nmiss)
+                                     int32_t *warp_sums, int32_t *nmiss, int32_t known)
 {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+    if (known >= 0) {  // posl already holds the position of every number (the listing warp's)
+        if (tid == 0) *nmiss = known;
+        resolve_outputs(posl, evt, os, om, cand, n, n0, nvis, dbs);
+        return;
+    }
     const int32_t nwords = (K + 31) >> 5;
     const int32_t per = (nwords + nt - 1) / nt;
     const int32_t w0 = min(tid * per, nwords), w1 = min(w0 + per, nwords);
@@ -659,19 +685,7 @@ __device__ void resolve_miss_numbers(const uint32_t *missb, int32_t K, uint16_t 
         for (uint32_t b = missb[w]; b; b &= b - 1u) posl[at++] = static_cast<uint16_t>((w << 5) + __ffs(b) - 1);
     }
     __syncthreads();
-    for (int32_t c = tid; c < dbs; c += nt) {
-        const uint16_t m = evt[c];
-        if (m == kNone16) continue;
-        const uint16_t pos = posl[m];
-        evt[c] = pos;
-        os[pos] = c;
-        om[pos] = 1;
-    }
-    for (int32_t sp = tid; sp < nvis; sp += nt) {
-        const int32_t i = n0 + sp >= n ? n0 + sp - n : n0 + sp;
-        const uint32_t x = cand[i];
-        cand[i] = (static_cast<uint32_t>(posl[x >> 16]) << 16) | (x & 0xFFFFu);
-    }
+    resolve_outputs(posl, evt, os, om, cand, n, n0, nvis, dbs);
 }
 
 // 2c: final visited bits of the slots passed: one slot per lane, one 32-slot word per warp
@@ -1023,7 +1037,7 @@ __device__ int32_t list_misses_in_order(const StepExtra &x, const int8_t *om, co
 __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n, const int32_t *tok,
                              const uint16_t *ht, uint32_t mask, int32_t padded, const int32_t *topk,
                              const uint32_t *missb, const uint16_t *nslot, const int32_t *prog, int32_t K, int32_t bid,
-                             uint16_t *hpos, int *verified, int *final_out)
+                             uint16_t *hpos, uint16_t *posl, int *verified, int *final_out)
 {
     const unsigned kAll = 0xFFFFFFFFu;
     const int htid = helper_index(threadIdx.x), lane = threadIdx.x & 31;
@@ -1097,7 +1111,11 @@ __device__ int32_t help_walk(const StepExtra &x, const uint32_t *cand, int32_t n
             if (ex < m1 && ex + pc > m0) {
                 int32_t num = ex;
                 for (uint32_t b = W; b != 0u && num < m1; b &= b - 1u, ++num)
-                    if (num >= m0) hpos[num - m0] = static_cast<uint16_t>((w + lane) * 32 + __ffs(b) - 1);
+                    if (num >= m0) {
+                        const uint16_t pos = static_cast<uint16_t>((w + lane) * 32 + __ffs(b) - 1);
+                        hpos[num - m0] = pos;
+                        posl[num] = pos;
+                    }
             }
             const unsigned reach = __ballot_sync(kAll, before + incl >= m1);
             if (reach != 0u) {  // the word holding number m1 - 1 is where the next batch starts
@@ -1597,14 +1615,15 @@ __global__ void __launch_bounds__(kFastThreads + (kMode == 1 ? 32 : 0), 1)
         if (is_walk_helper(tid)) {
             const int32_t hm = help_walk(x, s_cand, s_ncand, s_tok, s_ht, mask, padded, s_topk, s_missb,
                                          reinterpret_cast<const uint16_t *>(smem + L.nslot), s_prog, K, bid,
-                                         reinterpret_cast<uint16_t *>(smem + L.hpos), &s_hver, &s_hfinal);
+                                         reinterpret_cast<uint16_t *>(smem + L.hpos),
+                                         reinterpret_cast<uint16_t *>(smem + L.posl), &s_hver, &s_hfinal);
             if (tid == 32) s_hm = hm;
         }
     }
     __syncthreads();
     if (!s_flag)
         resolve_miss_numbers(s_missb, K, reinterpret_cast<uint16_t *>(smem + L.posl), s_evt, s_os, s_om, s_cand,
-                             s_ncand, s_n0, s_nvis, dbs, s_warp, &s_nkeys);
+                             s_ncand, s_n0, s_nvis, dbs, s_warp, &s_nkeys, s_hfinal ? s_hm : -1);
     __syncthreads();
     if (!s_flag && s_last >= 0) {
         passed_bits(s_vini, s_vfin, s_tf, s_evt, s_cand, s_wofs, s_ncand, dbs, s_hand, s_last);

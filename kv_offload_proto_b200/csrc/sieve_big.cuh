@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kBigThreads, 2) sieve_big_kernel(const SievePa
             __syncthreads();
             if (!s_flag)
                 resolve_miss_numbers(s_missb, K, s_posl, evt, s_os, s_om, cand, s_ncand, s_n0, s_nvis, dbs, s_warp,
-                                     &s_nkeys);
+                                     &s_nkeys, -1);
             __syncthreads();
             if (!s_flag && s_last >= 0) {
                 passed_bits(vini, vfin, tf, evt, cand, s_wofs, s_ncand, dbs, s_hand, s_last);
